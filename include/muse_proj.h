@@ -1,0 +1,127 @@
+/*
+ * muse_proj.h — C ABI of the B200 (sm_100a) BF16 projection library, libmuse_proj.so.
+ *
+ * y[M, N] = x[M, K] . W[N, K]^T with BF16 inputs, FP32 accumulation and a round-to-nearest-even
+ * BF16 output: the dense projection that the reference serves from kernel_fn
+ * (submission.py:1156-1170). Plain pointers and sizes only; every function returns MUSE_OK (0)
+ * or a negative MUSE_ERR_* code and never throws across the ABI; muse_last_error() gives the
+ * calling thread's last message. No function allocates device memory. Launches go on the
+ * stream given (a cudaStream_t passed as void*), so they can be captured in a CUDA graph.
+ *
+ * Pointers named x, w, y, planes, bases, esc_* in the muse_proj_* calls are DEVICE pointers;
+ * the muse_encode12 / muse_decode12 buffers are HOST pointers.
+ */
+#ifndef MUSE_PROJ_H
+#define MUSE_PROJ_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define MUSE_OK 0
+#define MUSE_ERR_INVALID (-1)   /* null pointer or non-positive size */
+#define MUSE_ERR_ALIGN (-2)     /* pointer not 16-byte aligned, or K * 2 bytes not a multiple of 16 */
+#define MUSE_ERR_SHAPE (-3)     /* shape outside what the chosen kernel supports */
+#define MUSE_ERR_CAPACITY (-4)  /* a caller-provided buffer is too small (see the count written) */
+#define MUSE_ERR_CUDA (-5)      /* a CUDA runtime / driver call failed (message has the name) */
+#define MUSE_ERR_TIMEOUT (-6)   /* a kernel's bounded wait expired (device error word was set) */
+#define MUSE_ERR_PLAN (-7)      /* unknown kernel id or plan field out of range */
+
+/* Kernels a plan can name. */
+#define MUSE_KERNEL_GEMV_BF16 1 /* streaming CUDA-core GEMV, BF16 W, M <= 8 */
+#define MUSE_KERNEL_GEMV_12B 2  /* streaming CUDA-core GEMV, 12-bit W, M <= 8 */
+#define MUSE_KERNEL_TC_TILE 3   /* tcgen05 128 x tile_n tiles, K split across a cluster */
+
+/* How one projection runs. Zero fields take the kernel's default. */
+typedef struct MusePlan {
+  int32_t kernel; /* MUSE_KERNEL_* */
+  int32_t split;  /* TC_TILE: CTAs of a cluster splitting K (1..16) */
+  int32_t tile_n; /* TC_TILE: tokens per tile, 16/32/64/128/256 */
+  int32_t stages; /* shared-memory ring depth (0 = as many as fit) */
+  int32_t ctas;   /* GEMV: CTAs in the grid (0 = one per SM) */
+  int32_t warps;  /* GEMV: consumer warps per CTA: 4, 8 or 16 (0 = 8) */
+  int32_t chunk;  /* GEMV: units per bulk copy (0 = about 16 KB) */
+  int32_t flags;  /* reserved, 0 */
+} MusePlan;
+
+/* A 12-bit encoded weight resident on the device (see muse_encode12 for the format). */
+typedef struct MuseEnc12 {
+  const uint8_t* planes;   /* N * K * 3 / 2 bytes */
+  const uint8_t* bases;    /* ceil(N / 128) * (K / 128) bytes */
+  const int32_t* esc_ptr;  /* N + 1 */
+  const uint32_t* esc_val; /* n_esc entries */
+  int64_t n, k, n_esc;
+} MuseEnc12;
+
+/* Library version string. */
+const char* muse_version(void);
+
+/* The calling thread's last error message ("" if none). */
+const char* muse_last_error(void);
+
+/* Number of SMs of the current device. */
+int muse_sm_count(int* out);
+
+/*
+ * Reads the device error word that bounded waits set on timeout, writes it to *code (0 = none)
+ * and clears it. Synchronizes `stream`. Returns MUSE_ERR_TIMEOUT when it was set.
+ * No counterpart in the reference (its kernels have no bounded waits).
+ */
+int muse_device_error(int* code, void* stream);
+
+/*
+ * The library's default plan for a shape (weights_12b: 1 when W is 12-bit encoded).
+ * Replaces the reference's per-shape tables' fallback rule (submission.py:76-127, 900-908):
+ * shapes no table row names get this plan.
+ */
+int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights_12b, MusePlan* out);
+
+/*
+ * y = x . W^T for BF16 W [N, K] (row-major, rows contiguous; W[:n] of a bigger matrix is the
+ * same pointer). Replaces, by plan->kernel:
+ *   MUSE_KERNEL_GEMV_BF16: the Triton split-K bf16_gemm (submission.py:1084-1107) at few tokens;
+ *   MUSE_KERNEL_TC_TILE:   TmaGemm.__call__ / wa_gemm (submission.py:977-988, 799-890) and the
+ *                          cuBLAS F.linear fallback (submission.py:1170; baseline.py:60).
+ * Needs x, w, y 16-byte aligned and K % 8 == 0 (GEMV: K % 256 == 0, M <= 8).
+ */
+int muse_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, const MusePlan* plan,
+                   void* stream);
+
+/*
+ * y = x . decode12(W)^T from the 12-bit planes. Replaces nf12_cuda_gemv / nf12_gemv
+ * (submission.py:660-673, 357-474). plan->kernel must be MUSE_KERNEL_GEMV_12B; M <= 8.
+ */
+int muse_proj_12b(const MuseEnc12* enc, const void* x, void* y, int64_t m, const MusePlan* plan, void* stream);
+
+/* Host buffer sizes for muse_encode12: planes and bases bytes. */
+int muse_encode12_sizes(int64_t n, int64_t k, int64_t* planes_bytes, int64_t* bases_bytes);
+
+/*
+ * Lossless 12-bit encoding of BF16 W [N, K] on the host (K % 512 == 0, K <= 65536).
+ * Replaces nf12_pack_cuda (submission.py:591-626), with the window base chosen per 128 x 128
+ * tile instead of once per matrix. Per tile, c0 = the first c maximising the count of weights
+ * whose high byte without sign (E7) lies in [c, c + 7]. A weight inside its tile's window keeps
+ * its low byte and a 4-bit code s << 3 | (E7 - c0); one outside is stored as zeros and listed as
+ * an escape. Layout: each row is K / 512 units of 768 bytes (512 low bytes, then 256 code bytes,
+ * byte j = code[2j] | code[2j+1] << 4); bases u8 [ceil(N/128)][K/128]; escapes a per-row CSR
+ * (esc_ptr[N + 1]) of u32 entries k << 16 | true BF16 bits. Writes the escape count to *n_esc;
+ * returns MUSE_ERR_CAPACITY (with *n_esc set) when esc_cap is too small. threads <= 0: all cores.
+ */
+int muse_encode12(const uint16_t* w, int64_t n, int64_t k, uint8_t* planes, uint8_t* bases, int32_t* esc_ptr,
+                  uint32_t* esc_val, int64_t esc_cap, int64_t* n_esc, int threads);
+
+/*
+ * Host decode of the 12-bit format back to BF16 bits [N, K] (the round-trip check the reference
+ * runs as an assert in nf12_pack_cuda, submission.py:611-617).
+ */
+int muse_decode12(const uint8_t* planes, const uint8_t* bases, const int32_t* esc_ptr, const uint32_t* esc_val,
+                  int64_t n, int64_t k, uint16_t* w_out, int threads);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MUSE_PROJ_H */

@@ -1,0 +1,132 @@
+"""ctypes binding of libmuse_proj.so (the C ABI declared in include/muse_proj.h).
+
+The library is built in-tree (``python -m muse_bf16_proj_b200.build``). There is no fallback:
+if the library is missing or fails to load, every projection raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+from .build import LIB
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "muse_proj.h")
+
+MUSE_OK = 0
+ERRORS = {-1: "INVALID", -2: "ALIGN", -3: "SHAPE", -4: "CAPACITY", -5: "CUDA", -6: "TIMEOUT", -7: "PLAN"}
+KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE = 1, 2, 3
+KERNEL_NAMES = {KERNEL_GEMV_BF16: "gemv_bf16", KERNEL_GEMV_12B: "gemv_12b", KERNEL_TC_TILE: "tc_tile"}
+KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
+
+
+class MuseError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"muse error {code} ({ERRORS.get(code, '?')}): {message}")
+        self.code = code
+
+
+class MusePlan(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int32) for name in
+                ("kernel", "split", "tile_n", "stages", "ctas", "warps", "chunk", "flags")]
+
+    def as_dict(self) -> dict:
+        d = {name: int(getattr(self, name)) for name, _ in self._fields_}
+        d["kernel"] = KERNEL_NAMES.get(d["kernel"], d["kernel"])
+        return d
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "MusePlan":
+        p = cls()
+        for name, _ in cls._fields_:
+            v = d.get(name, 0)
+            if name == "kernel" and isinstance(v, str):
+                v = KERNEL_IDS[v]
+            setattr(p, name, int(v))
+        return p
+
+    def key(self) -> tuple:
+        return tuple(int(getattr(self, name)) for name, _ in self._fields_)
+
+
+class MuseEnc12(ctypes.Structure):
+    _fields_ = [("planes", ctypes.c_void_p), ("bases", ctypes.c_void_p), ("esc_ptr", ctypes.c_void_p),
+                ("esc_val", ctypes.c_void_p), ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("n_esc", ctypes.c_int64)]
+
+
+_lib = None
+
+_P, _I64, _I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+_SIGNATURES = {
+    "muse_version": ([], ctypes.c_char_p),
+    "muse_last_error": ([], ctypes.c_char_p),
+    "muse_sm_count": ([ctypes.POINTER(ctypes.c_int)], _I32),
+    "muse_device_error": ([ctypes.POINTER(ctypes.c_int), _P], _I32),
+    "muse_plan_default": ([_I64, _I64, _I64, _I32, ctypes.POINTER(MusePlan)], _I32),
+    "muse_proj_bf16": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P], _I32),
+    "muse_proj_12b": ([ctypes.POINTER(MuseEnc12), _P, _P, _I64, ctypes.POINTER(MusePlan), _P], _I32),
+    "muse_encode12_sizes": ([_I64, _I64, ctypes.POINTER(_I64), ctypes.POINTER(_I64)], _I32),
+    "muse_encode12": ([_P, _I64, _I64, _P, _P, _P, _P, _I64, ctypes.POINTER(_I64), _I32], _I32),
+    "muse_decode12": ([_P, _P, _P, _P, _I64, _I64, _P, _I32], _I32),
+}
+
+
+def declared_symbols() -> list[str]:
+    """Function names declared in include/muse_proj.h."""
+    with open(HEADER) as f:
+        text = f.read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(muse_\w+)\s*\(", text, flags=re.M)))
+
+
+def load():
+    """The loaded library (loads it on first use). Raises if it is not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            raise RuntimeError(f"{LIB} is not built: run `python -m muse_bf16_proj_b200.build` (no fallback path exists)")
+        lib = ctypes.CDLL(LIB)
+        for name, (args, res) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = lib
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != MUSE_OK:
+        raise MuseError(rc, load().muse_last_error().decode(errors="replace"))
+
+
+def version() -> str:
+    return load().muse_version().decode()
+
+
+def sm_count() -> int:
+    out = ctypes.c_int()
+    check(load().muse_sm_count(ctypes.byref(out)))
+    return out.value
+
+
+def device_error(stream: int = 0) -> int:
+    """The device error word (0 = none), cleared afterwards. Raises MuseError when it was set."""
+    code = ctypes.c_int()
+    rc = load().muse_device_error(ctypes.byref(code), ctypes.c_void_p(stream))
+    if rc != MUSE_OK:
+        raise MuseError(rc, load().muse_last_error().decode(errors="replace"))
+    return code.value
+
+
+def plan_default(m: int, n: int, k: int, weights_12b: bool = False) -> MusePlan:
+    p = MusePlan()
+    check(load().muse_plan_default(m, n, k, int(weights_12b), ctypes.byref(p)))
+    return p
+
+
+def proj_bf16(x_ptr: int, w_ptr: int, y_ptr: int, m: int, n: int, k: int, plan: MusePlan, stream: int) -> None:
+    check(load().muse_proj_bf16(x_ptr, w_ptr, y_ptr, m, n, k, ctypes.byref(plan), ctypes.c_void_p(stream)))
+
+
+def proj_12b(enc: MuseEnc12, x_ptr: int, y_ptr: int, m: int, plan: MusePlan, stream: int) -> None:
+    check(load().muse_proj_12b(ctypes.byref(enc), x_ptr, y_ptr, m, ctypes.byref(plan), ctypes.c_void_p(stream)))

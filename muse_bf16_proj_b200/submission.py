@@ -1,0 +1,197 @@
+"""The drop-in entry point for the BF16 dense projections: ``prepare(weights)`` once, untimed, then
+``kernel_fn(data, state)`` per call (the reference's interface, submission.py:23-41, 1115-1173).
+
+What serves each shape (``kernel_fn`` -> ``project``), chosen per (N, K, M) by the committed sweep
+table (``dispatch.py``), else by the library's default plan:
+
+- few tokens, BF16 W: the streaming CUDA-core GEMV (bulk-copy shared-memory ring, deterministic
+  split-K inside the CTA);
+- few tokens, 12-bit W: the same GEMV reading the lossless 12-bit planes (about 12 bits a weight);
+- more tokens: the tcgen05/TMEM tile kernel, with K split across a thread-block cluster and
+  reduced over DSMEM in a fixed order for skinny shapes.
+
+All three are this build's own sm_100a kernels behind the C ABI in include/muse_proj.h. There is
+no cuBLAS, Triton or CPU fallback: a shape the kernels cannot run raises.
+
+``prepare`` keeps every BF16 weight resident, builds 12-bit copies of the layers the table serves
+from 12 bits (host encoder, checked lossless bit for bit), and runs a known-answer self-check of
+every planned kernel: one-hot power-of-two rows of x must return exact columns of W (the
+reference's probe-row idea, reference.py:30-35), so a wrong kernel raises in prepare instead of
+serving (the reference instead fell back to Triton/cuBLAS, submission.py:1142-1151).
+
+The FP32 router (reference submission.py:130-205, 1027-1076) is outside this build's BF16 path:
+``kernel_fn`` raises NotImplementedError for it.
+"""
+
+from __future__ import annotations
+
+from typing import TypedDict
+
+import numpy as np
+import torch
+
+from . import _lib, codec12
+from .contract import UNPOOL_SLICE, SLICED_MAX_TOKENS
+from .dispatch import Dispatch
+
+
+class Weights(TypedDict):
+    qkv_gate: torch.Tensor  # bfloat16 [2304, 8192]
+    o: torch.Tensor         # bfloat16 [8192, 1024]
+    pooler: torch.Tensor    # bfloat16 [4096, 8192]
+    unpooler: torch.Tensor  # bfloat16 [8192, 4096]; up to 8 tokens, only rows 0-1023 (this GPU's slice)
+    router: torch.Tensor    # float32 [256, 8192] (not served by this build)
+
+
+class Config(TypedDict):
+    m: int
+    n: int      # output width; the unpooler's is 1024 up to 8 tokens (this GPU's slice), else 8192
+    k: int
+    layer: str  # which weight
+
+
+class Inputs(TypedDict):
+    x: torch.Tensor  # bfloat16 [M, K]
+    config: Config
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+class _Enc12Device:
+    """A 12-bit encoded weight resident on the device, with C-ABI views per output width n."""
+
+    def __init__(self, enc: codec12.Encoded12, device: torch.device):
+        self.n, self.k, self.n_esc = enc.n, enc.k, enc.n_esc
+        self.planes = torch.from_numpy(enc.planes).to(device)
+        self.bases = torch.from_numpy(enc.bases.reshape(-1)).to(device)
+        self.esc_ptr = torch.from_numpy(enc.esc_ptr).to(device)
+        self.esc_val = torch.from_numpy(enc.esc_val.view(np.int32) if enc.n_esc else np.zeros(1, np.int32)).to(device)
+        self.escape_fraction = enc.escape_fraction
+        self._esc_ptr_host = enc.esc_ptr
+        self._views: dict = {}
+
+    def view(self, n: int) -> _lib.MuseEnc12:
+        v = self._views.get(n)
+        if v is None:
+            v = _lib.MuseEnc12(self.planes.data_ptr(), self.bases.data_ptr(), self.esc_ptr.data_ptr(),
+                               self.esc_val.data_ptr(), n, self.k, int(self._esc_ptr_host[n]))
+            self._views[n] = v
+        return v
+
+    @property
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.planes, self.bases, self.esc_ptr, self.esc_val))
+
+
+def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | None = None,
+            self_check: bool = True, verbose: bool = True) -> dict:
+    """Builds the state kernel_fn serves from. ``weights``: name -> W [N, K] on the GPU (BF16;
+    FP32 entries are kept but not served). ``encode_12b`` forces (True) or forbids (False) the
+    12-bit copies; None lets the dispatch table decide."""
+    _lib.load()
+    disp = dispatch if dispatch is not None else Dispatch()
+    state = {"weights": {}, "fp32": {}, "enc12": {}, "dispatch": disp, "checked": []}
+    for name, w in weights.items():
+        if w.dtype != torch.bfloat16:
+            state["fp32"][name] = w.contiguous()
+            continue
+        if w.dim() != 2 or not w.is_cuda:
+            raise ValueError(f"{name}: expected a 2-D CUDA tensor, got {tuple(w.shape)} on {w.device}")
+        w = w.contiguous()
+        state["weights"][name] = w
+        n, k = w.shape
+        widths = [n] + ([UNPOOL_SLICE] if name == "unpooler" and n > UNPOOL_SLICE else [])
+        want = encode_12b if encode_12b is not None else any(disp.wants_12b(nn, k) for nn in widths)
+        if want and k % codec12.UNIT == 0 and k <= 65536:
+            enc = codec12.encode(_bits(w))  # raises if the round trip is not bit-exact
+            if enc.escape_fraction > codec12.MAX_ESCAPE_FRACTION:
+                if verbose:
+                    print(f"muse: {name}: {enc.escape_fraction:.3%} escapes, kept BF16 only")
+            else:
+                state["enc12"][name] = _Enc12Device(enc, w.device)
+                if verbose:
+                    print(f"muse: {name}: 12-bit planes, {enc.n_esc} escapes ({enc.escape_fraction:.4%})")
+    if self_check:
+        for name, w in state["weights"].items():
+            n, k = w.shape
+            for nn, ms in _check_points(name, n, k, disp):
+                for m in ms:
+                    _known_answer_check(state, name, nn, m)
+                    state["checked"].append((name, nn, m))
+    torch.cuda.synchronize()
+    return state
+
+
+def _check_points(name: str, n: int, k: int, disp: Dispatch):
+    """(n, [m, ...]) pairs the self-check runs: each table row's range ends, plus 1 and 16."""
+    widths = [n] + ([UNPOOL_SLICE] if name == "unpooler" and n > UNPOOL_SLICE else [])
+    out = []
+    for nn in widths:
+        ms = {1, 16} if nn == n else {1, SLICED_MAX_TOKENS}
+        for lo, hi, _ in disp.ms_for(nn, k):
+            ms.update({lo, min(hi, 256)})
+        if nn == UNPOOL_SLICE and name == "unpooler":
+            ms = {m for m in ms if m <= SLICED_MAX_TOKENS}
+        out.append((nn, sorted(ms)))
+    return out
+
+
+def _known_answer_check(state: dict, layer: str, n: int, m: int) -> None:
+    """x = one-hot rows (value 2^p at a spread column): y row i must be 2^p * W[:n, c_i]."""
+    w = state["weights"][layer]
+    k = w.shape[1]
+    dev = w.device
+    cols = (torch.arange(m, device=dev) * 7919 + 17) % k
+    powers = 2.0 ** (torch.arange(m, device=dev) % 5)
+    x = torch.zeros((m, k), dtype=torch.float32, device=dev)
+    x[torch.arange(m, device=dev), cols] = powers
+    x = x.to(torch.bfloat16)
+    y = project(x, state, layer, n).float()
+    expect = (w[:n].float()[:, cols].T * powers[:, None]).to(torch.bfloat16).float()
+    plan, fmt = state["dispatch"].plan(m, n, k, layer in state["enc12"])
+    if fmt == "12b":
+        err = ((y - expect).norm(dim=1) / expect.norm(dim=1).clamp(min=1e-30)).max().item()
+        ok = err <= 1e-3
+    else:
+        ok = torch.equal(y, expect) or bool(((y == expect) | (torch.isnan(y) & torch.isnan(expect))).all())
+        err = (y - expect).abs().max().item()
+    code = _lib.device_error(torch.cuda.current_stream(dev).cuda_stream)
+    if not ok or code:
+        raise RuntimeError(f"muse self-check failed: {layer} n={n} m={m} plan={plan.as_dict()} {fmt}: "
+                           f"err {err:.3e}, device error {code:#x}")
+
+
+def project(x: torch.Tensor, state: dict, layer: str, n: int | None = None,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ W[:n].T (BF16 [m, n]) on this build's kernels."""
+    w = state["weights"].get(layer)
+    if w is None:
+        if layer in state["fp32"]:
+            raise NotImplementedError(f"{layer}: FP32 weights are outside this build's BF16 projection path")
+        raise KeyError(layer)
+    big_n, k = w.shape
+    n = big_n if n is None else n
+    if x.dim() != 2 or x.shape[1] != k or x.dtype != torch.bfloat16 or not (0 < n <= big_n):
+        raise ValueError(f"{layer}: x {tuple(x.shape)} {x.dtype}, n={n} does not match W {tuple(w.shape)}")
+    if not x.is_contiguous():
+        x = x.contiguous()
+    if x.data_ptr() % 16:
+        x = x.clone()  # the kernels read x with 16-byte vector loads / TMA
+    m = x.shape[0]
+    enc = state["enc12"].get(layer)
+    plan, fmt = state["dispatch"].plan(m, n, k, enc is not None)
+    y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    if fmt == "12b":
+        _lib.proj_12b(enc.view(n), x.data_ptr(), y.data_ptr(), m, plan, stream)
+    else:
+        _lib.proj_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, plan, stream)
+    return y
+
+
+def kernel_fn(data: Inputs, state) -> torch.Tensor:
+    """data["x"] [m, k] BF16 @ W[:n].T -> [m, n] BF16, for data["config"]["layer"]."""
+    cfg = data["config"]
+    return project(data["x"], state, cfg["layer"], cfg["n"])

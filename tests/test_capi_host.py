@@ -1,0 +1,81 @@
+"""The C ABI without a GPU: the library loads, exports every declared symbol, and rejects bad
+arguments with its documented error codes before touching the device."""
+
+import ctypes
+
+import pytest
+
+from muse_bf16_proj_b200 import _lib
+from muse_bf16_proj_b200.dispatch import Dispatch
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = _lib.declared_symbols()
+    assert len(names) >= 10
+    for name in names:
+        assert hasattr(lib, name), name
+    assert _lib.version().startswith("muse_proj_b200")
+
+
+def test_declared_signatures_are_bound():
+    assert set(_lib.declared_symbols()) == set(_lib._SIGNATURES)
+
+
+def test_proj_argument_errors_before_any_device_work():
+    lib = _lib.load()
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, split=1, tile_n=16)
+    p = ctypes.byref(plan)
+    assert lib.muse_proj_bf16(None, 16, 16, 1, 128, 64, p, None) == -1
+    assert lib.muse_proj_bf16(16, 16, 16, 0, 128, 64, p, None) == -1
+    assert lib.muse_proj_bf16(18, 16, 16, 1, 128, 64, p, None) == -2   # x misaligned
+    assert lib.muse_proj_bf16(16, 16, 16, 1, 128, 60, p, None) == -2   # K * 2 not a multiple of 16
+    assert lib.muse_proj_bf16(16, 16, 16, 1, 128, 64, None, None) == -1
+    enc = _lib.MuseEnc12(16, 16, 16, 16, 128, 512, 0)
+    plan12 = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE)
+    assert lib.muse_proj_12b(ctypes.byref(enc), 16, 16, 1, ctypes.byref(plan12), None) == -7
+    enc_bad = _lib.MuseEnc12(None, 16, 16, 16, 128, 512, 0)
+    assert lib.muse_proj_12b(ctypes.byref(enc_bad), 16, 16, 1, ctypes.byref(plan12), None) == -1
+    assert b"null" in lib.muse_last_error()
+
+
+def test_plan_default_without_device():
+    p = _lib.plan_default(1, 6144, 4096)
+    assert p.kernel == _lib.KERNEL_GEMV_BF16
+    p = _lib.plan_default(16, 6144, 4096)
+    assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 16 and 1 <= p.split <= 8
+    p = _lib.plan_default(4096, 10240, 8192)
+    assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 256 and p.split == 1
+    p = _lib.plan_default(1, 10240, 8192, weights_12b=True)
+    assert p.kernel == _lib.KERNEL_GEMV_12B
+    with pytest.raises(_lib.MuseError):
+        _lib.plan_default(0, 10, 10)
+
+
+def test_dispatch_table_lookup_and_defaults():
+    entries = [
+        {"n": 6144, "k": 4096, "m_lo": 1, "m_hi": 1, "weights": "12b", "plan": {"kernel": "gemv_12b", "warps": 8}},
+        {"n": 6144, "k": 4096, "m_lo": 1, "m_hi": 4, "weights": "bf16", "plan": {"kernel": "gemv_bf16", "warps": 16}},
+        {"n": 6144, "k": 4096, "m_lo": 5, "m_hi": 32, "plan": {"kernel": "tc_tile", "tile_n": 32, "split": 3}},
+    ]
+    d = Dispatch(entries=entries)
+    plan, fmt = d.plan(1, 6144, 4096, have_12b=True)
+    assert fmt == "12b" and plan.kernel == _lib.KERNEL_GEMV_12B
+    plan, fmt = d.plan(1, 6144, 4096, have_12b=False)
+    assert fmt == "bf16" and plan.kernel == _lib.KERNEL_GEMV_BF16 and plan.warps == 16
+    plan, fmt = d.plan(17, 6144, 4096)
+    assert plan.kernel == _lib.KERNEL_TC_TILE and plan.split == 3 and plan.tile_n == 32
+    plan, fmt = d.plan(64, 6144, 4096)   # no row: library default
+    assert plan.kernel == _lib.KERNEL_TC_TILE and plan.tile_n == 64
+    assert d.wants_12b(6144, 4096) and not d.wants_12b(6144, 8192)
+    assert _lib.MusePlan.from_dict(plan.as_dict()).key() == plan.key()
+
+
+def test_committed_table_rows_are_valid():
+    d = Dispatch()
+    for e in d.entries:
+        p = _lib.MusePlan.from_dict(e["plan"])
+        assert p.kernel in _lib.KERNEL_NAMES
+        assert e["m_lo"] <= e["m_hi"]
+        if p.kernel == _lib.KERNEL_GEMV_12B:
+            assert e["weights"] == "12b"
