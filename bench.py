@@ -284,19 +284,17 @@ def main():
         torch.cuda.synchronize()
 
     K = args.steps
-    ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     # Keep the GPU busy while the host enqueues every step, so the timed region holds no host gaps.
+    # Only the region's two events: an event between steps would stop the next projection's
+    # programmatic launch from overlapping the previous one, as it does in a serving stream.
     torch.cuda._sleep(int(min(2e9, (K * (enqueue_s + 20e-6) + 2e-3) * 2.0e9)))
     start.record(stream)
     for i in range(K):
-        ev_s[i].record(stream)
         step(i)
-        ev_e[i].record(stream)
         if gather_out is not None:
             dist.all_gather_into_tensor(gather_out, ys[i % rot])
     end.record(stream)
@@ -305,13 +303,13 @@ def main():
         dist.barrier()
     clocks = sampler.stop()
     total_ms = start.elapsed_time(end)
-    launch_ms = [ev_s[i].elapsed_time(ev_e[i]) for i in range(K)]
     if world > 1:
-        t = torch.tensor([total_ms, statistics.mean(launch_ms)], device=dev, dtype=torch.float64)
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, mean_launch_ms = float(t[0]), float(t[1])
-    else:
-        mean_launch_ms = statistics.mean(launch_ms)
+        total_ms = float(t[0])
+    # One projection kernel per step: its launch-to-launch time is the step time.
+    mean_launch_ms = total_ms / K
+    isolated_us = isolated_latency_us(step, rot, stream)
     code = _lib.device_error(stream.cuda_stream)
 
     # ---- e2e through kernel_fn with host buffers --------------------------------------------
@@ -343,12 +341,14 @@ def main():
     roof["peak_source"] = f"{peaks_kind} (MEASURED_PEAKS.json)" if peaks_kind == "measured" else "fallback"
     roof["kernel"] = kernel_name
     roof["mean_launch_us"] = round(mean_launch_ms * 1e3, 3)
+    roof["launch_time"] = "timed region / steps (one projection kernel per step, launched back to back)"
     roof["traffic"] = traffic_from_profiles(kernel_name, args.workload)
     roof["spec_frac"] = round(achieved / (8000.0 if hbm_bound else 2250.0), 4)
 
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": unit, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(per_step_ms, 6), "latency_us": round(per_step_ms * 1e3, 3),
+        "isolated_launch_us": round(isolated_us, 3),
         "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
         "dtype": "bf16" if fmt == "bf16" else "bf16 (12-bit lossless weights)",
         "data": "synthetic: seeded x ~ N(0,1) with the reference's probe rows, W ~ N(0,0.02)"
@@ -374,6 +374,24 @@ def main():
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def isolated_latency_us(step, rot, stream, reps: int = 20) -> float:
+    """Median time of ONE projection launch with nothing queued around it and its weights cold
+    in L2 (the next copy of the rotation), as the reference's judge times a call (its ~4 us graph
+    replay cost is not subtracted here)."""
+    import torch
+
+    times = []
+    for i in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(stream)
+        step(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    return statistics.median(times)
 
 
 def run_e2e(state, names, layer, m, n, k, rot, K, dev, world, bytes_step, flops_step):

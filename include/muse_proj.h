@@ -33,18 +33,26 @@ extern "C" {
 /* Kernels a plan can name. */
 #define MUSE_KERNEL_GEMV_BF16 1 /* streaming CUDA-core GEMV, BF16 W, M <= 8 */
 #define MUSE_KERNEL_GEMV_12B 2  /* streaming CUDA-core GEMV, 12-bit W, M <= 8 */
-#define MUSE_KERNEL_TC_TILE 3   /* tcgen05 128 x tile_n tiles, K split across a cluster */
+#define MUSE_KERNEL_TC_TILE 3   /* tcgen05 128 x tile_n tiles, K split across a cluster or through scratch */
+#define MUSE_KERNEL_TC_STREAMK 4 /* tcgen05 stream-K over packed tiles: equal work per CTA, one wave */
+
+/* Plan flags. */
+#define MUSE_FLAG_GLOBAL_SPLIT 1 /* TC_TILE: reduce K-split partials through caller scratch instead of a cluster */
+/* Programmatic dependent launch: the kernel may start while the previous kernel in the stream
+ * finishes; it streams its first weights before waiting for that kernel, and touches x, y and
+ * scratch only after. Only for weights that the preceding kernel in the stream does not write. */
+#define MUSE_FLAG_PDL 2
 
 /* How one projection runs. Zero fields take the kernel's default. */
 typedef struct MusePlan {
   int32_t kernel; /* MUSE_KERNEL_* */
-  int32_t split;  /* TC_TILE: CTAs of a cluster splitting K (1..16) */
+  int32_t split;  /* TC_TILE: CTAs splitting K (cluster: 1..16; global: 1..64) */
   int32_t tile_n; /* TC_TILE: tokens per tile, 16/32/64/128/256 */
-  int32_t stages; /* shared-memory ring depth (0 = as many as fit) */
-  int32_t ctas;   /* GEMV: CTAs in the grid (0 = one per SM) */
+  int32_t stages; /* shared-memory ring depth (0 = kernel default) */
+  int32_t ctas;   /* GEMV, TC_STREAMK: CTAs in the grid (0 = one per SM) */
   int32_t warps;  /* GEMV: consumer warps per CTA: 4, 8 or 16 (0 = 8) */
   int32_t chunk;  /* GEMV: units per bulk copy (0 = about 16 KB) */
-  int32_t flags;  /* reserved, 0 */
+  int32_t flags;  /* MUSE_FLAG_* */
 } MusePlan;
 
 /* A 12-bit encoded weight resident on the device (see muse_encode12 for the format). */
@@ -55,6 +63,15 @@ typedef struct MuseEnc12 {
   const uint32_t* esc_val; /* n_esc entries */
   int64_t n, k, n_esc;
 } MuseEnc12;
+
+/*
+ * Per-CTA timestamp trace for the launches that follow (debug / profiling aid; NULL turns it
+ * off). `records` is a device buffer of `capacity` 48-byte records, one per CTA (CTAs past the
+ * capacity are not traced): u64 globaltimer ns at kernel entry, after the prologue, after the
+ * main loop, at exit; u32 SM id; u32 CTA index; 8 bytes padding. Process-wide setting.
+ * No counterpart in the reference (it profiled through its judge's kernel table).
+ */
+int muse_set_trace(void* records, int64_t capacity);
 
 /* Library version string. */
 const char* muse_version(void);
@@ -80,15 +97,50 @@ int muse_device_error(int* code, void* stream);
 int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights_12b, MusePlan* out);
 
 /*
+ * Bytes of device scratch a plan needs (0 for most plans). Scratch holds the per-tile split-K
+ * counters (first 64 KB) and FP32 partials of MUSE_FLAG_GLOBAL_SPLIT plans. The caller zeroes it
+ * once; every launch leaves the counters at zero again (after a device error, zero it again).
+ * Launches that share one scratch buffer must not overlap in time (use one per stream).
+ * No counterpart in the reference beyond its split-K counters (submission.py:112, 1126).
+ */
+int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, int64_t* bytes);
+
+/*
  * y = x . W^T for BF16 W [N, K] (row-major, rows contiguous; W[:n] of a bigger matrix is the
  * same pointer). Replaces, by plan->kernel:
  *   MUSE_KERNEL_GEMV_BF16: the Triton split-K bf16_gemm (submission.py:1084-1107) at few tokens;
  *   MUSE_KERNEL_TC_TILE:   TmaGemm.__call__ / wa_gemm (submission.py:977-988, 799-890) and the
  *                          cuBLAS F.linear fallback (submission.py:1170; baseline.py:60).
- * Needs x, w, y 16-byte aligned and K % 8 == 0 (GEMV: K % 256 == 0, M <= 8).
+ * Needs x, w, y 16-byte aligned and K % 8 == 0 (GEMV: K % 256 == 0, M <= 8). scratch may be NULL
+ * when muse_scratch_bytes reports 0.
  */
 int muse_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, const MusePlan* plan,
-                   void* stream);
+                   void* scratch, int64_t scratch_bytes, void* stream);
+
+/*
+ * Bytes of the packed-tile copy of W [N, K] made by muse_pack_tiles:
+ * ceil(N / 128) * ceil(K / 64) * 16384.
+ */
+int muse_tiles_bytes(int64_t n, int64_t k, int64_t* bytes);
+
+/*
+ * Repacks row-major BF16 W [N, K] (device) into contiguous 16 KB tiles of 128 rows x 64 k, each in
+ * the 128-byte-swizzled order the tensor cores read, zero-padded at the edges (device kernel on
+ * `stream`). Lossless. Replaces pack_w_tiles (submission.py:926-934), which packed 64 * wg-row
+ * tiles for the Hopper kernel.
+ */
+int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stream);
+
+/*
+ * y = x . W^T with W given as packed tiles (muse_pack_tiles of the full W: the first
+ * ceil(n / 128) row tiles serve W[:n]). plan->kernel: MUSE_KERNEL_TC_TILE or
+ * MUSE_KERNEL_TC_STREAMK (which always needs scratch, see muse_scratch_bytes). Each pipeline
+ * stage moves one contiguous 16 KB tile with a 1-D bulk copy. Replaces TmaGemm.__call__
+ * (submission.py:977-988), which read its pre-swizzled W the same way, and the Triton split-K
+ * bf16_gemm with its atomic tile tickets (submission.py:209-251, 1084-1107).
+ */
+int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
+                         const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream);
 
 /*
  * y = x . decode12(W)^T from the 12-bit planes. Replaces nf12_cuda_gemv / nf12_gemv

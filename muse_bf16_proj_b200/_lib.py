@@ -16,9 +16,13 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 
 MUSE_OK = 0
 ERRORS = {-1: "INVALID", -2: "ALIGN", -3: "SHAPE", -4: "CAPACITY", -5: "CUDA", -6: "TIMEOUT", -7: "PLAN"}
-KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE = 1, 2, 3
-KERNEL_NAMES = {KERNEL_GEMV_BF16: "gemv_bf16", KERNEL_GEMV_12B: "gemv_12b", KERNEL_TC_TILE: "tc_tile"}
+KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE, KERNEL_TC_STREAMK = 1, 2, 3, 4
+KERNEL_NAMES = {KERNEL_GEMV_BF16: "gemv_bf16", KERNEL_GEMV_12B: "gemv_12b", KERNEL_TC_TILE: "tc_tile",
+                KERNEL_TC_STREAMK: "tc_streamk"}
+TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK)
 KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
+FLAG_GLOBAL_SPLIT = 1
+FLAG_PDL = 2
 
 
 class MuseError(RuntimeError):
@@ -64,7 +68,12 @@ _SIGNATURES = {
     "muse_sm_count": ([ctypes.POINTER(ctypes.c_int)], _I32),
     "muse_device_error": ([ctypes.POINTER(ctypes.c_int), _P], _I32),
     "muse_plan_default": ([_I64, _I64, _I64, _I32, ctypes.POINTER(MusePlan)], _I32),
-    "muse_proj_bf16": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P], _I32),
+    "muse_scratch_bytes": ([_I64, _I64, _I64, ctypes.POINTER(MusePlan), ctypes.POINTER(_I64)], _I32),
+    "muse_proj_bf16": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
+    "muse_tiles_bytes": ([_I64, _I64, ctypes.POINTER(_I64)], _I32),
+    "muse_set_trace": ([_P, _I64], _I32),
+    "muse_pack_tiles": ([_P, _P, _I64, _I64, _P], _I32),
+    "muse_proj_bf16_tiles": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
     "muse_proj_12b": ([ctypes.POINTER(MuseEnc12), _P, _P, _I64, ctypes.POINTER(MusePlan), _P], _I32),
     "muse_encode12_sizes": ([_I64, _I64, ctypes.POINTER(_I64), ctypes.POINTER(_I64)], _I32),
     "muse_encode12": ([_P, _I64, _I64, _P, _P, _P, _P, _I64, ctypes.POINTER(_I64), _I32], _I32),
@@ -83,9 +92,10 @@ def load():
     """The loaded library (loads it on first use). Raises if it is not built."""
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB):
-            raise RuntimeError(f"{LIB} is not built: run `python -m muse_bf16_proj_b200.build` (no fallback path exists)")
-        lib = ctypes.CDLL(LIB)
+        path = os.environ.get("MUSE_PROJ_LIB", LIB)
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is not built: run `python -m muse_bf16_proj_b200.build` (no fallback path exists)")
+        lib = ctypes.CDLL(path)
         for name, (args, res) in _SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = args
@@ -124,9 +134,41 @@ def plan_default(m: int, n: int, k: int, weights_12b: bool = False) -> MusePlan:
     return p
 
 
-def proj_bf16(x_ptr: int, w_ptr: int, y_ptr: int, m: int, n: int, k: int, plan: MusePlan, stream: int) -> None:
-    check(load().muse_proj_bf16(x_ptr, w_ptr, y_ptr, m, n, k, ctypes.byref(plan), ctypes.c_void_p(stream)))
+def proj_bf16(x_ptr: int, w_ptr: int, y_ptr: int, m: int, n: int, k: int, plan: MusePlan, stream: int,
+              scratch_ptr: int = 0, scratch_bytes: int = 0) -> None:
+    check(load().muse_proj_bf16(x_ptr, w_ptr, y_ptr, m, n, k, ctypes.byref(plan), scratch_ptr or None, scratch_bytes,
+                                ctypes.c_void_p(stream)))
+
+
+def proj_bf16_tiles(x_ptr: int, tiles_ptr: int, y_ptr: int, m: int, n: int, k: int, plan: MusePlan, stream: int,
+                    scratch_ptr: int = 0, scratch_bytes: int = 0) -> None:
+    check(load().muse_proj_bf16_tiles(x_ptr, tiles_ptr, y_ptr, m, n, k, ctypes.byref(plan), scratch_ptr or None,
+                                      scratch_bytes, ctypes.c_void_p(stream)))
+
+
+def scratch_bytes(m: int, n: int, k: int, plan: MusePlan) -> int:
+    out = ctypes.c_int64()
+    check(load().muse_scratch_bytes(m, n, k, ctypes.byref(plan), ctypes.byref(out)))
+    return out.value
+
+
+def tiles_bytes(n: int, k: int) -> int:
+    out = ctypes.c_int64()
+    check(load().muse_tiles_bytes(n, k, ctypes.byref(out)))
+    return out.value
+
+
+def pack_tiles(w_ptr: int, tiles_ptr: int, n: int, k: int, stream: int) -> None:
+    check(load().muse_pack_tiles(w_ptr, tiles_ptr, n, k, ctypes.c_void_p(stream)))
 
 
 def proj_12b(enc: MuseEnc12, x_ptr: int, y_ptr: int, m: int, plan: MusePlan, stream: int) -> None:
     check(load().muse_proj_12b(ctypes.byref(enc), x_ptr, y_ptr, m, ctypes.byref(plan), ctypes.c_void_p(stream)))
+
+
+TRACE_RECORD_BYTES = 48
+
+
+def set_trace(ptr: int, capacity: int) -> None:
+    """Per-CTA timestamps for later launches into a device buffer (ptr 0 turns tracing off)."""
+    check(load().muse_set_trace(ptr or None, capacity))

@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libmuse_proj.so")
 SOURCES = ["capi.cu", "codec12.cpp"]
-HEADERS = ["ptx.cuh", "gemv.cuh", "tc_tile.cuh", "errors.h"]
+HEADERS = ["ptx.cuh", "gemv.cuh", "tc_tile.cuh", "tc_streamk.cuh", "errors.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -38,13 +38,16 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 
-def build(force: bool = False, ptxas_verbose: bool = False) -> str:
-    if not force and not _stale():
+def build(force: bool = False, ptxas_verbose: bool = False, out: str | None = None, defines=()) -> str:
+    """Compiles the library (to `out` instead of the package's lib/ when given, with extra
+    -D`defines`, e.g. for timing a variant side by side)."""
+    target = out or LIB
+    if out is None and not force and not _stale():
         return LIB
-    os.makedirs(LIB_DIR, exist_ok=True)
-    tmp = LIB + ".tmp"
+    os.makedirs(os.path.dirname(target), exist_ok=True)
+    tmp = target + ".tmp"
     cmd = [nvcc_path(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-shared", "-Xcompiler", "-fPIC,-O3",
-           "-o", tmp] + [os.path.join(CSRC, s) for s in SOURCES] + ["-lpthread"]
+           "-o", tmp] + [f"-D{d}" for d in defines] + [os.path.join(CSRC, s) for s in SOURCES] + ["-lpthread"]
     if ptxas_verbose:
         cmd += ["-Xptxas", "-v"]
     proc = subprocess.run(cmd, cwd=CSRC, capture_output=True, text=True)
@@ -52,8 +55,8 @@ def build(force: bool = False, ptxas_verbose: bool = False) -> str:
         raise RuntimeError(f"nvcc failed ({proc.returncode}):\n{proc.stdout}\n{proc.stderr}")
     if ptxas_verbose:
         sys.stderr.write(proc.stderr)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, target)
+    return target
 
 
 if __name__ == "__main__":

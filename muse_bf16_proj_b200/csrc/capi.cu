@@ -8,12 +8,14 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/muse_proj.h"
 #include "errors.h"
 #include "gemv.cuh"
 #include "tc_tile.cuh"
+#include "tc_streamk.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -89,6 +91,10 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Optional per-CTA trace buffer for the next launches (muse_set_trace); off when null.
+std::atomic<muse::TraceRec*> g_trace{nullptr};
+std::atomic<int> g_trace_cap{0};
+
 int launch_error(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
@@ -98,7 +104,7 @@ int launch_error(const char* what) {
 // ---- GEMV ------------------------------------------------------------------------------------
 
 template <bool kTwelve, int M, int NW>
-int launch_gemv_t(const muse::GemvArgs& a, int grid, int smem, cudaStream_t st) {
+int launch_gemv_t(const muse::GemvArgs& a, int grid, int smem, bool pdl, cudaStream_t st) {
   auto kern = muse::gemv_stream_kernel<kTwelve, M, NW>;
   static bool configured[kMaxDevices] = {};
   int dev;
@@ -108,31 +114,42 @@ int launch_gemv_t(const muse::GemvArgs& a, int grid, int smem, cudaStream_t st) 
     if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(gemv): %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
-  kern<<<grid, 32 * (NW + 1), smem, st>>>(a);
-  return launch_error("gemv launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(32 * (NW + 1), 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "gemv launch: %s", cudaGetErrorString(e));
+  return MUSE_OK;
 }
 
 template <bool kTwelve, int M>
-int launch_gemv_m(const muse::GemvArgs& a, int warps, int grid, int smem, cudaStream_t st) {
+int launch_gemv_m(const muse::GemvArgs& a, int warps, int grid, int smem, bool pdl, cudaStream_t st) {
   switch (warps) {
-    case 4: return launch_gemv_t<kTwelve, M, 4>(a, grid, smem, st);
-    case 8: return launch_gemv_t<kTwelve, M, 8>(a, grid, smem, st);
-    case 16: return launch_gemv_t<kTwelve, M, 16>(a, grid, smem, st);
+    case 4: return launch_gemv_t<kTwelve, M, 4>(a, grid, smem, pdl, st);
+    case 8: return launch_gemv_t<kTwelve, M, 8>(a, grid, smem, pdl, st);
+    case 16: return launch_gemv_t<kTwelve, M, 16>(a, grid, smem, pdl, st);
     default: return fail(MUSE_ERR_PLAN, "gemv: warps must be 4, 8 or 16 (got %d)", warps);
   }
 }
 
 template <bool kTwelve>
-int launch_gemv(const muse::GemvArgs& a, int m, int warps, int grid, int smem, cudaStream_t st) {
+int launch_gemv(const muse::GemvArgs& a, int m, int warps, int grid, int smem, bool pdl, cudaStream_t st) {
   switch (m) {
-    case 1: return launch_gemv_m<kTwelve, 1>(a, warps, grid, smem, st);
-    case 2: return launch_gemv_m<kTwelve, 2>(a, warps, grid, smem, st);
-    case 3: return launch_gemv_m<kTwelve, 3>(a, warps, grid, smem, st);
-    case 4: return launch_gemv_m<kTwelve, 4>(a, warps, grid, smem, st);
-    case 5: return launch_gemv_m<kTwelve, 5>(a, warps, grid, smem, st);
-    case 6: return launch_gemv_m<kTwelve, 6>(a, warps, grid, smem, st);
-    case 7: return launch_gemv_m<kTwelve, 7>(a, warps, grid, smem, st);
-    case 8: return launch_gemv_m<kTwelve, 8>(a, warps, grid, smem, st);
+    case 1: return launch_gemv_m<kTwelve, 1>(a, warps, grid, smem, pdl, st);
+    case 2: return launch_gemv_m<kTwelve, 2>(a, warps, grid, smem, pdl, st);
+    case 3: return launch_gemv_m<kTwelve, 3>(a, warps, grid, smem, pdl, st);
+    case 4: return launch_gemv_m<kTwelve, 4>(a, warps, grid, smem, pdl, st);
+    case 5: return launch_gemv_m<kTwelve, 5>(a, warps, grid, smem, pdl, st);
+    case 6: return launch_gemv_m<kTwelve, 6>(a, warps, grid, smem, pdl, st);
+    case 7: return launch_gemv_m<kTwelve, 7>(a, warps, grid, smem, pdl, st);
+    case 8: return launch_gemv_m<kTwelve, 8>(a, warps, grid, smem, pdl, st);
     default: return fail(MUSE_ERR_SHAPE, "gemv: M must be 1..8 (got %d)", m);
   }
 }
@@ -170,6 +187,8 @@ int plan_gemv(bool twelve, int64_t m, int64_t n, int64_t k, const MusePlan& p, m
       a.rows_per_cta = static_cast<int>(rows);
       a.chunk_units = chunk;
       a.stages = stages;
+      a.trace = g_trace.load();
+      a.trace_cap = a.trace ? g_trace_cap.load() : 0;
       *grid = static_cast<int>((n + rows - 1) / rows);
       *smem = static_cast<int>(stages * chunk_bytes + 16 * stages + red);
       return MUSE_OK;
@@ -181,47 +200,16 @@ int plan_gemv(bool twelve, int64_t m, int64_t n, int64_t k, const MusePlan& p, m
 
 // ---- tcgen05 tile kernel ---------------------------------------------------------------------
 
-template <int BNT>
-int launch_tc_t(const CUtensorMap& tmw, const CUtensorMap& tmx, uint16_t* y, int m, int n, int k, int split,
-                int stages, cudaStream_t st) {
-  auto kern = muse::tc_tile_kernel<BNT>;
-  const int smem = muse::tc_tile_smem(BNT, stages);
-  static bool configured[kMaxDevices] = {};
-  int dev;
-  if (int rc = current_device(&dev)) return rc;
-  cudaError_t e = cudaSuccess;
-  if (!configured[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_tile): %s", cudaGetErrorString(e));
-    configured[dev] = true;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(((n + 127) / 128) * split), static_cast<unsigned>((m + BNT - 1) / BNT), 1);
-  cfg.blockDim = dim3(muse::kTcThreads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(split);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (split > 1) {
-    int clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
-    if (e != cudaSuccess || clusters < 1)
-      return fail(MUSE_ERR_PLAN, "tc_tile: clusters of %d CTAs with %d B shared memory cannot be scheduled (%s)", split,
-                  smem, e == cudaSuccess ? "occupancy 0" : cudaGetErrorString(e));
-  }
-  e = cudaLaunchKernelEx(&cfg, kern, tmw, tmx, y, m, n, k, split, stages);
-  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_tile launch (split %d, tile %d): %s", split, BNT, cudaGetErrorString(e));
-  return MUSE_OK;
-}
+constexpr int64_t kCounterBytes = 64 * 1024;  // per-tile split-K counters at the front of scratch
+constexpr int64_t kMaxCounters = kCounterBytes / 4;
 
-int run_tc_tile(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p,
-                cudaStream_t st) {
+struct TcShape {
+  int bnt, split, stages, mode;
+  int64_t tiles;          // output tiles (row tiles x token tiles)
+  int64_t partial_bytes;  // global split: tiles * split * bnt * 128 * 4
+};
+
+int tc_shape(int64_t m, int64_t n, int64_t k, const MusePlan& p, TcShape* out) {
   DeviceInfo* d;
   if (int rc = device_info(&d)) return rc;
   int bnt = p.tile_n;
@@ -233,29 +221,233 @@ int run_tc_tile(const void* x, const void* w, void* y, int64_t m, int64_t n, int
     return fail(MUSE_ERR_PLAN, "tc_tile: tile_n must be 16, 32, 64, 128 or 256 (got %d)", bnt);
   const int nkb = static_cast<int>((k + muse::kTcBK - 1) / muse::kTcBK);
   const int split = p.split > 0 ? p.split : 1;
-  if (split > 16 || split > nkb)
-    return fail(MUSE_ERR_PLAN, "tc_tile: split %d must be <= 16 and <= K / 64 = %d", split, nkb);
+  const bool global = (p.flags & MUSE_FLAG_GLOBAL_SPLIT) != 0;
+  if (split > (global ? 64 : 16) || split > nkb)
+    return fail(MUSE_ERR_PLAN, "tc_tile: split %d must be <= %d and <= K / 64 = %d", split, global ? 64 : 16, nkb);
   if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
     return fail(MUSE_ERR_SHAPE, "tc_tile: dimension too large");
   const int limit = std::min(kSmemLimit, d->smem_optin);
   const int per_stage = muse::kTcABytes + muse::tc_tile_bbytes(bnt);
-  int max_stages = (limit - 1024 - 64) / (per_stage + 16);
-  int stages = p.stages > 0 ? p.stages : max_stages;
-  if (stages > max_stages || stages < 2) return fail(MUSE_ERR_PLAN, "tc_tile: %d stages do not fit (max %d)", stages, max_stages);
-  // The FP32 partial [tile_n][128] reuses the ring; it must fit there.
-  if (split > 1 && bnt * 128 * 4 > stages * per_stage)
+  const int max_stages = (limit - 1024 - 64) / (per_stage + 16);
+  const int stages = p.stages > 0 ? p.stages : max_stages;
+  if (stages > max_stages || stages < 2)
+    return fail(MUSE_ERR_PLAN, "tc_tile: %d stages do not fit (max %d)", stages, max_stages);
+  if (split > 1 && !global && bnt * 128 * 4 > stages * per_stage)
     return fail(MUSE_ERR_PLAN, "tc_tile: ring of %d stages too small for the split-K partial", stages);
+  out->bnt = bnt;
+  out->split = split;
+  out->stages = stages;
+  out->mode = global && split > 1 ? muse::kTcModeGlobalSplit : 0;
+  out->tiles = ((n + 127) / 128) * ((m + bnt - 1) / bnt);
+  out->partial_bytes = (out->mode & muse::kTcModeGlobalSplit) ? out->tiles * split * bnt * 128 * 4 : 0;
+  if ((out->mode & muse::kTcModeGlobalSplit) && out->tiles > kMaxCounters)
+    return fail(MUSE_ERR_SHAPE, "tc_tile: %lld output tiles exceed the %lld split-K counters", (long long)out->tiles,
+                (long long)kMaxCounters);
+  return MUSE_OK;
+}
+
+int64_t tc_scratch_bytes(const TcShape& s) { return s.partial_bytes ? kCounterBytes + s.partial_bytes : 0; }
+
+template <int BNT>
+int launch_tc_t(const CUtensorMap& tmw, const CUtensorMap& tmx, const muse::TcArgs& a, int m, int n, bool pdl,
+                cudaStream_t st) {
+  auto kern = muse::tc_tile_kernel<BNT>;
+  const int smem = muse::tc_tile_smem(BNT, a.stages);
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaError_t e = cudaSuccess;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_tile): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  const bool cluster = a.split > 1 && !(a.mode & muse::kTcModeGlobalSplit);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(((n + 127) / 128) * a.split), static_cast<unsigned>((m + BNT - 1) / BNT), 1);
+  cfg.blockDim = dim3(muse::kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster ? a.split : 1);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (cluster) {
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess || clusters < 1)
+      return fail(MUSE_ERR_PLAN, "tc_tile: clusters of %d CTAs with %d B shared memory cannot be scheduled (%s)",
+                  a.split, smem, e == cudaSuccess ? "occupancy 0" : cudaGetErrorString(e));
+  }
+  e = cudaLaunchKernelEx(&cfg, kern, tmw, tmx, a);
+  if (e != cudaSuccess)
+    return fail(MUSE_ERR_CUDA, "tc_tile launch (split %d, tile %d): %s", a.split, BNT, cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
+// W is row-major (tiles == nullptr) or packed tiles (w == nullptr).
+int run_tc_tile(const void* x, const void* w, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
+                const MusePlan& p, void* scratch, int64_t scratch_bytes, cudaStream_t st) {
+  TcShape sh;
+  if (int rc = tc_shape(m, n, k, p, &sh)) return rc;
+  const int64_t need = tc_scratch_bytes(sh);
+  if (need > 0 && (!scratch || scratch_bytes < need))
+    return fail(MUSE_ERR_CAPACITY, "tc_tile: global split-K needs %lld bytes of zeroed scratch (got %lld)",
+                (long long)need, (long long)(scratch ? scratch_bytes : 0));
+  if (need > 0 && (reinterpret_cast<uintptr_t>(scratch) & 255u))
+    return fail(MUSE_ERR_ALIGN, "tc_tile: scratch must be 256-byte aligned");
   CUtensorMap tmw, tmx;
-  if (int rc = make_map(&tmw, w, n, k, 128)) return rc;
-  if (int rc = make_map(&tmx, x, m, k, bnt)) return rc;
-  auto yy = static_cast<uint16_t*>(y);
-  const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
-  switch (bnt) {
-    case 16: return launch_tc_t<16>(tmw, tmx, yy, mi, ni, ki, split, stages, st);
-    case 32: return launch_tc_t<32>(tmw, tmx, yy, mi, ni, ki, split, stages, st);
-    case 64: return launch_tc_t<64>(tmw, tmx, yy, mi, ni, ki, split, stages, st);
-    case 128: return launch_tc_t<128>(tmw, tmx, yy, mi, ni, ki, split, stages, st);
-    default: return launch_tc_t<256>(tmw, tmx, yy, mi, ni, ki, split, stages, st);
+  std::memset(&tmw, 0, sizeof(tmw));
+  if (!tiles) {
+    if (int rc = make_map(&tmw, w, n, k, 128)) return rc;
+  }
+  if (int rc = make_map(&tmx, x, m, k, sh.bnt)) return rc;
+  muse::TcArgs a;
+  a.wtiles = static_cast<const uint8_t*>(tiles);
+  a.y = static_cast<uint16_t*>(y);
+  a.counters = need > 0 ? static_cast<int*>(scratch) : nullptr;
+  a.partials = need > 0 ? reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kCounterBytes) : nullptr;
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.K = static_cast<int>(k);
+  a.split = sh.split;
+  a.stages = sh.stages;
+  a.mode = sh.mode | (tiles ? muse::kTcModeTiles : 0);
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  const int mi = static_cast<int>(m), ni = static_cast<int>(n);
+  // Programmatic launch only for grids without clusters.
+  const bool pdl = (p.flags & MUSE_FLAG_PDL) != 0 && !(sh.split > 1 && !(sh.mode & muse::kTcModeGlobalSplit));
+  switch (sh.bnt) {
+    case 16: return launch_tc_t<16>(tmw, tmx, a, mi, ni, pdl, st);
+    case 32: return launch_tc_t<32>(tmw, tmx, a, mi, ni, pdl, st);
+    case 64: return launch_tc_t<64>(tmw, tmx, a, mi, ni, pdl, st);
+    case 128: return launch_tc_t<128>(tmw, tmx, a, mi, ni, pdl, st);
+    default: return launch_tc_t<256>(tmw, tmx, a, mi, ni, pdl, st);
+  }
+}
+
+// ---- stream-K tcgen05 kernel -----------------------------------------------------------------
+
+struct SkShape {
+  int bnt, stages, g, smax;
+  int rtiles, nkb, ttiles;
+  long long units, tiles;
+  int64_t scratch;
+};
+
+int sk_shape(int64_t m, int64_t n, int64_t k, const MusePlan& p, SkShape* out) {
+  DeviceInfo* d;
+  int sms = 148, limit = kSmemLimit;
+  if (device_info(&d) == MUSE_OK) {
+    sms = d->sms;
+    limit = std::min(kSmemLimit, d->smem_optin);
+  }
+  muse::clear_error();
+  int bnt = p.tile_n;
+  if (bnt == 0) {
+    bnt = 16;
+    while (bnt < m && bnt < 128) bnt *= 2;
+  }
+  if (bnt != 16 && bnt != 32 && bnt != 64 && bnt != 128 && bnt != 256)
+    return fail(MUSE_ERR_PLAN, "tc_streamk: tile_n must be 16, 32, 64, 128 or 256 (got %d)", bnt);
+  if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "tc_streamk: dimension too large");
+  const int per_stage = 16384 + muse::sk_bbytes(bnt);
+  const int max_stages = (limit - 1024 - 96) / (per_stage + 16);
+  const int stages = p.stages > 0 ? p.stages : std::min(6, max_stages);
+  if (stages < 2 || stages > max_stages)
+    return fail(MUSE_ERR_PLAN, "tc_streamk: %d stages do not fit (max %d)", stages, max_stages);
+  SkShape sh;
+  sh.bnt = bnt;
+  sh.stages = stages;
+  sh.rtiles = static_cast<int>((n + 127) / 128);
+  sh.nkb = static_cast<int>((k + 63) / 64);
+  sh.ttiles = static_cast<int>((m + bnt - 1) / bnt);
+  sh.tiles = static_cast<long long>(sh.rtiles) * sh.ttiles;
+  sh.units = sh.tiles * sh.nkb;
+  if (sh.tiles > kMaxCounters)
+    return fail(MUSE_ERR_SHAPE, "tc_streamk: %lld output tiles exceed the %lld counters", sh.tiles, (long long)kMaxCounters);
+  long long g = p.ctas > 0 ? p.ctas : sms;
+  g = std::min<long long>(g, sh.units);
+  sh.g = static_cast<int>(g);
+  int smax = 1;
+  for (long long t = 0; t < sh.tiles; ++t) {
+    const int a0 = muse::sk_owner(t * sh.nkb, sh.units, sh.g);
+    const int a1 = muse::sk_owner((t + 1) * sh.nkb - 1, sh.units, sh.g);
+    smax = std::max(smax, a1 - a0 + 1);
+  }
+  sh.smax = smax;
+  sh.scratch = kCounterBytes + static_cast<int64_t>(sh.tiles) * smax * bnt * 128 * 4;
+  *out = sh;
+  return MUSE_OK;
+}
+
+template <int BNT>
+int launch_sk_t(const CUtensorMap& tmx, const muse::SkArgs& a, int g, bool pdl, cudaStream_t st) {
+  auto kern = muse::tc_streamk_kernel<BNT>;
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_streamk): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(g), 1, 1);
+  cfg.blockDim = dim3(muse::kSkThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(muse::sk_smem(BNT, a.stages));
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmx, a);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_streamk launch (tile %d): %s", BNT, cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
+int run_streamk(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p,
+                void* scratch, int64_t scratch_bytes, cudaStream_t st) {
+  SkShape sh;
+  if (int rc = sk_shape(m, n, k, p, &sh)) return rc;
+  if (!scratch || scratch_bytes < sh.scratch)
+    return fail(MUSE_ERR_CAPACITY, "tc_streamk: needs %lld bytes of zeroed scratch (got %lld)", (long long)sh.scratch,
+                (long long)(scratch ? scratch_bytes : 0));
+  if (reinterpret_cast<uintptr_t>(scratch) & 255u) return fail(MUSE_ERR_ALIGN, "tc_streamk: scratch must be 256-byte aligned");
+  CUtensorMap tmx;
+  if (int rc = make_map(&tmx, x, m, k, sh.bnt)) return rc;
+  muse::SkArgs a;
+  a.wtiles = static_cast<const uint8_t*>(tiles);
+  a.y = static_cast<uint16_t*>(y);
+  a.counters = static_cast<int*>(scratch);
+  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kCounterBytes);
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.K = static_cast<int>(k);
+  a.stages = sh.stages;
+  a.rtiles = sh.rtiles;
+  a.nkb = sh.nkb;
+  a.ttiles = sh.ttiles;
+  a.units = sh.units;
+  a.smax = sh.smax;
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  const bool pdl = (p.flags & MUSE_FLAG_PDL) != 0;
+  switch (sh.bnt) {
+    case 16: return launch_sk_t<16>(tmx, a, sh.g, pdl, st);
+    case 32: return launch_sk_t<32>(tmx, a, sh.g, pdl, st);
+    case 64: return launch_sk_t<64>(tmx, a, sh.g, pdl, st);
+    case 128: return launch_sk_t<128>(tmx, a, sh.g, pdl, st);
+    default: return launch_sk_t<256>(tmx, a, sh.g, pdl, st);
   }
 }
 
@@ -321,8 +513,71 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights_12b, MusePlan
   return MUSE_OK;
 }
 
+int muse_set_trace(void* records, int64_t capacity) {
+  muse::clear_error();
+  if (records && capacity < 1) return fail(MUSE_ERR_INVALID, "set_trace: capacity must be positive");
+  if (records && (reinterpret_cast<uintptr_t>(records) & 15u)) return fail(MUSE_ERR_ALIGN, "set_trace: 16-byte alignment");
+  g_trace_cap.store(records ? static_cast<int>(std::min<int64_t>(capacity, 1 << 30)) : 0);
+  g_trace.store(static_cast<muse::TraceRec*>(records));
+  return MUSE_OK;
+}
+
+int muse_tiles_bytes(int64_t n, int64_t k, int64_t* bytes) {
+  muse::clear_error();
+  if (!bytes) return fail(MUSE_ERR_INVALID, "tiles_bytes: null output");
+  if (n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "tiles_bytes: non-positive size");
+  *bytes = ((n + 127) / 128) * ((k + 63) / 64) * int64_t(muse::kTcABytes);
+  return MUSE_OK;
+}
+
+int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stream) {
+  muse::clear_error();
+  if (!w || !tiles) return fail(MUSE_ERR_INVALID, "pack_tiles: null pointer");
+  if (n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "pack_tiles: non-positive size");
+  if (!aligned16(w) || !aligned16(tiles) || k % 8) return fail(MUSE_ERR_ALIGN, "pack_tiles: 16-byte alignment and K % 8 == 0 needed");
+  if (n > (int64_t(1) << 24) || k > (int64_t(1) << 24)) return fail(MUSE_ERR_SHAPE, "pack_tiles: dimension too large");
+  const int nkb = static_cast<int>((k + 63) / 64);
+  const long long chunks = ((n + 127) / 128) * static_cast<long long>(nkb) * 1024;
+  const int blocks = static_cast<int>(std::min<long long>((chunks + 255) / 256, 148 * 32));
+  muse::pack_tiles_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(w), static_cast<uint4*>(tiles), static_cast<int>(n), static_cast<int>(k), nkb, chunks);
+  return launch_error("pack_tiles launch");
+}
+
+int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, int64_t* bytes) {
+  muse::clear_error();
+  if (!plan || !bytes) return fail(MUSE_ERR_INVALID, "scratch_bytes: null pointer");
+  if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "scratch_bytes: non-positive size");
+  *bytes = 0;
+  if (plan->kernel == MUSE_KERNEL_TC_STREAMK) {
+    SkShape sk;
+    if (int rc = sk_shape(m, n, k, *plan, &sk)) return rc;
+    *bytes = sk.scratch;
+    return MUSE_OK;
+  }
+  if (plan->kernel != MUSE_KERNEL_TC_TILE) return MUSE_OK;
+  TcShape sh;
+  if (int rc = tc_shape(m, n, k, *plan, &sh)) return rc;
+  *bytes = tc_scratch_bytes(sh);
+  return MUSE_OK;
+}
+
+int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
+                         const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream) {
+  muse::clear_error();
+  if (!x || !tiles || !y || !plan) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles: null pointer");
+  if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles: non-positive size");
+  if (!aligned16(x) || !aligned16(tiles) || (reinterpret_cast<uintptr_t>(y) & 1u) || (k * 2) % 16)
+    return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles: x and tiles 16-byte aligned, y 2-byte aligned, K % 8 == 0");
+  if (plan->kernel == MUSE_KERNEL_TC_STREAMK)
+    return run_streamk(x, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
+  if (plan->kernel != MUSE_KERNEL_TC_TILE)
+    return fail(MUSE_ERR_PLAN, "proj_bf16_tiles: plan kernel must be TC_TILE or TC_STREAMK");
+  return run_tc_tile(x, nullptr, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
+}
+
 int muse_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, const MusePlan* plan,
-                   void* stream) {
+                   void* scratch, int64_t scratch_bytes, void* stream) {
   muse::clear_error();
   if (!x || !w || !y || !plan) return fail(MUSE_ERR_INVALID, "proj_bf16: null pointer");
   if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "proj_bf16: non-positive size");
@@ -338,9 +593,9 @@ int muse_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, 
     a.k = static_cast<int>(k);
     int grid, smem, warps;
     if (int rc = plan_gemv(false, m, n, k, *plan, a, &grid, &smem, &warps)) return rc;
-    return launch_gemv<false>(a, static_cast<int>(m), warps, grid, smem, st);
+    return launch_gemv<false>(a, static_cast<int>(m), warps, grid, smem, (plan->flags & MUSE_FLAG_PDL) != 0, st);
   }
-  if (plan->kernel == MUSE_KERNEL_TC_TILE) return run_tc_tile(x, w, y, m, n, k, *plan, st);
+  if (plan->kernel == MUSE_KERNEL_TC_TILE) return run_tc_tile(x, w, nullptr, y, m, n, k, *plan, scratch, scratch_bytes, st);
   return fail(MUSE_ERR_PLAN, "proj_bf16: kernel %d does not take BF16 weights", plan->kernel);
 }
 
@@ -363,7 +618,8 @@ int muse_proj_12b(const MuseEnc12* enc, const void* x, void* y, int64_t m, const
   a.k = static_cast<int>(enc->k);
   int grid, smem, warps;
   if (int rc = plan_gemv(true, m, enc->n, enc->k, *plan, a, &grid, &smem, &warps)) return rc;
-  return launch_gemv<true>(a, static_cast<int>(m), warps, grid, smem, static_cast<cudaStream_t>(stream));
+  return launch_gemv<true>(a, static_cast<int>(m), warps, grid, smem, (plan->flags & MUSE_FLAG_PDL) != 0,
+                           static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

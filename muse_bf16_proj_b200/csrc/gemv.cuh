@@ -24,6 +24,8 @@ struct GemvArgs {
   const int32_t* esc_ptr;   // 12-bit: per-row CSR [N + 1]
   const uint32_t* esc_val;  // 12-bit: k << 16 | true BF16 bits
   int n, k, rows_per_cta, chunk_units, stages;
+  TraceRec* trace;   // optional per-CTA timestamps (nullptr: off)
+  int trace_cap;
 };
 
 template <bool kTwelve>
@@ -127,6 +129,8 @@ template <bool kTwelve, int M, int NW>
 __global__ void __launch_bounds__(32 * (NW + 1), 1) gemv_stream_kernel(const GemvArgs a) {
   using F = GemvFormat<kTwelve>;
   extern __shared__ __align__(128) uint8_t smem[];
+  const bool tracing = a.trace != nullptr && static_cast<int>(blockIdx.x) < a.trace_cap && threadIdx.x == 0;
+  unsigned long long t_start = tracing ? globaltimer() : 0ull, t_ready = 0ull, t_main = 0ull;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * a.rows_per_cta;
@@ -149,6 +153,7 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1) gemv_stream_kernel(const Gem
     fence_mbar_init();
   }
   __syncthreads();
+  if (tracing) t_ready = globaltimer();
 
   if (warp == NW) {
     // Producer: one lane streams this CTA's contiguous byte range.
@@ -171,7 +176,8 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1) gemv_stream_kernel(const Gem
         mbar_wait(&full[c % a.stages], (c / a.stages) & 1, kErrDrain, kWaitLimitNs / 10);
     }
   } else {
-    // Consumers.
+    // Consumers. x (and y, written at the end) may belong to the grid this one overlaps with.
+    pdl_wait();
     for (int c = 0; c < nchunks; ++c) {
       const int s = c % a.stages;
       // Warp-uniform, so no lane leaves the loop while others still shuffle.
@@ -193,8 +199,10 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1) gemv_stream_kernel(const Gem
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
+    if (tracing) t_main = globaltimer();
   }
   __syncthreads();
+  pdl_launch_dependents();  // every thread: the weights are consumed, the next grid may start
 
   // Fixed-order sum of each row's segments (then 12-bit escape corrections) and the BF16 store;
   // consecutive threads take consecutive rows of one token.
@@ -219,6 +227,7 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1) gemv_stream_kernel(const Gem
     }
     a.y[static_cast<size_t>(m) * a.n + r0 + row] = f32_to_bf16(sum);
   }
+  if (tracing) a.trace[blockIdx.x] = TraceRec{t_start, t_ready, t_main, globaltimer(), smid(), blockIdx.x, 0u, 0u};
 }
 
 }  // namespace muse

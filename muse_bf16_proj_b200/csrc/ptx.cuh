@@ -37,6 +37,21 @@ __device__ __forceinline__ bool error_raised() {
   return *reinterpret_cast<volatile unsigned int*>(&g_dev_error) != 0u;
 }
 
+// ---- per-CTA timestamp trace (off unless the host set a buffer) -----------------------------
+
+// One record per CTA: globaltimer (ns) at entry, after the prologue, when its main loop's last
+// data has been consumed, and at exit; plus the SM it ran on.
+struct TraceRec {
+  unsigned long long t_start, t_ready, t_mainloop, t_end;
+  unsigned int smid, block, pad0, pad1;
+};
+
+__device__ __forceinline__ unsigned int smid() {
+  unsigned int r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
+
 // ---- mbarrier ------------------------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -56,8 +71,14 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
+// Phase test. MUSE_WAIT_MODE 0: try_wait (may suspend up to the system time limit),
+// 1: try_wait with a 200 ns suspend hint, 2: test_wait (never suspends).
+#ifndef MUSE_WAIT_MODE
+#define MUSE_WAIT_MODE 2
+#endif
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t ok;
+#if MUSE_WAIT_MODE == 0
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
@@ -65,6 +86,23 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
       : "=r"(ok)
       : "r"(bar), "r"(parity)
       : "memory");
+#elif MUSE_WAIT_MODE == 1
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 200;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+#else
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+#endif
   return ok != 0;
 }
 
@@ -90,6 +128,51 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   const uint32_t b = smem_u32(bar);
   if (mbar_test(b, parity)) return true;
   return mbar_wait_slow(b, parity, where, limit_ns);
+}
+
+// ---- programmatic dependent launch -------------------------------------------------------------
+
+// Waits until the grids this one depends on (launched before it in the stream) have completed and
+// their memory is visible. Returns at once when the launch was not programmatic.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the next programmatic launch in the stream start scheduling its CTAs.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- split-K tickets ---------------------------------------------------------------------------
+
+// Called by one thread after a barrier that follows every partial store of its group: publishes
+// the group's partials (release, cumulative over the barrier) and takes a ticket; returns the
+// ticket value, with acquire semantics so the reducer sees every earlier contributor's partial.
+__device__ __forceinline__ int ticket_acq_rel(int* counter) {
+  int old;
+  asm volatile("fence.acq_rel.gpu;\n\tatom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+  return old;
+}
+
+// Sum of `n` FP32 partials of 16 values each, laid out `stride` floats apart with value j at
+// +j * 128, added in index order; the loads of 4 partials at a time are in flight together.
+__device__ __forceinline__ void sum_partials16(const float* base, int n, size_t stride, float (&sum)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) sum[j] = 0.f;
+  for (int p0 = 0; p0 < n; p0 += 4) {
+    float v[4][16];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      if (p0 + p < n) {
+        const float* src = base + static_cast<size_t>(p0 + p) * stride;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[p][j] = __ldcg(src + j * 128);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      if (p0 + p < n) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum[j] += v[p][j];
+      }
+    }
+  }
 }
 
 // ---- L2 cache policies -----------------------------------------------------------------------
@@ -154,7 +237,7 @@ __device__ __forceinline__ uint32_t map_peer(uint32_t local_smem, uint32_t rank)
 
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
   return v;
 }
 

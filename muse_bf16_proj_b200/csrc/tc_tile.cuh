@@ -1,16 +1,24 @@
 // tcgen05 tile GEMM with W as the UMMA A operand: y[m, n] = sum_k x[m, k] * W[n, k].
 //
-// One CTA computes a 128 (rows of W) x BNT (tokens) FP32 tile in TMEM over a K range. W and x
-// both stay K-major in global memory and arrive by 2-D TMA (128-byte swizzle, no multicast) into
-// a `stages`-deep shared-memory ring; one thread issues the UMMAs (M = 128, N = BNT, K = 16);
-// four epilogue warps read the accumulator back with tcgen05.ld.
+// One CTA computes a 128 (rows of W) x BNT (tokens) FP32 tile in TMEM over a K range. x arrives
+// by 2-D TMA (128-byte swizzle, no multicast) and W either
+//   - from "tiles": W repacked once (muse_pack_tiles) into contiguous 16 KB blocks
+//     [N/128][K/64][128 rows][64 k], each already in the 128-byte-swizzled order the UMMA
+//     descriptor reads, so a stage is ONE 1-D bulk copy of 16 contiguous KB (the DRAM-friendly
+//     way to stream W), or
+//   - from the row-major W by 2-D TMA boxes of 128 rows x 128 bytes (no repacking needed).
+// One thread issues the UMMAs (M = 128, N = BNT, K = 16); four epilogue warps read the
+// accumulator back with tcgen05.ld.
 //
-// Split-K: the `split` CTAs of a thread-block cluster take consecutive K ranges of the same tile.
-// Each parks its FP32 partial in its own shared memory; after a cluster barrier, CTA r sums the
-// tokens j = r, r + split, ... over all peers' partials through DSMEM in rank order 0..split-1 and
-// stores BF16. One launch, no global scratch, deterministic.
+// Split-K, two ways, both deterministic (partials summed in rank order 0..split-1):
+//   - cluster: the `split` CTAs of a thread-block cluster take consecutive K ranges; each parks its
+//     FP32 partial in its own shared memory and CTA r sums tokens r, r + split, ... over the peers
+//     through DSMEM. No global scratch; needs the whole cluster co-resident.
+//   - global: each CTA writes its partial to caller scratch and bumps a per-tile counter; the CTA
+//     that arrives last sums all partials and resets the counter to 0 (counters start at 0 and
+//     every launch leaves them at 0). No co-scheduling constraint.
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + UMMA issuer,
+// Warp roles (192 threads): warp 0 = producer, warp 1 = TMEM owner + UMMA issuer,
 // warps 2..5 = epilogue (warp w reads TMEM lanes 32 * (w % 4) .. + 31).
 #pragma once
 
@@ -22,6 +30,9 @@ constexpr int kTcThreads = 192;
 constexpr int kTcBK = 64;                   // K elements per stage (128 bytes of BF16)
 constexpr int kTcABytes = 128 * kTcBK * 2;  // 16 KB: 128 W rows
 
+constexpr int kTcModeTiles = 1;        // W given as packed tiles
+constexpr int kTcModeGlobalSplit = 2;  // K-split partials reduced through global scratch
+
 __host__ __device__ constexpr int tc_tile_bbytes(int bnt) { return bnt * kTcBK * 2; }
 __host__ __device__ constexpr int tc_tile_tmem_cols(int bnt) { return bnt < 32 ? 32 : bnt; }
 
@@ -30,35 +41,71 @@ __host__ __device__ constexpr int tc_tile_smem(int bnt, int stages) {
   return 1024 + stages * (kTcABytes + tc_tile_bbytes(bnt)) + (2 * stages + 1) * 8 + 16;
 }
 
+struct TcArgs {
+  const uint8_t* wtiles;  // packed tiles (mode & kTcModeTiles)
+  uint16_t* y;            // [M, N]
+  float* partials;        // global split: [tiles][split][BNT][128]
+  int* counters;          // global split: [tiles], zero between launches
+  int M, N, K, split, stages, mode;
+  TraceRec* trace;  // optional per-CTA timestamps (nullptr: off)
+  int trace_cap;
+};
+
+// Packed-tile layout: tile (rt, kb) = 16 KB at ((rt * nkb) + kb) * 16384; row r of the tile at
+// r * 128; the 16-byte chunk holding k = kb * 64 + c * 8 .. + 7 at chunk position c ^ (r % 8).
+// Rows >= N and columns >= K are zero. One thread per 16-byte output chunk.
+__global__ void pack_tiles_kernel(const uint16_t* __restrict__ w, uint4* __restrict__ out, int n, int k, int nkb,
+                                  long long chunks) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < chunks;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long tile = i >> 10;
+    const int within = static_cast<int>(i & 1023);
+    const int r = within >> 3;
+    const int c = (within & 7) ^ (r & 7);
+    const int rt = static_cast<int>(tile / nkb), kb = static_cast<int>(tile % nkb);
+    const int row = rt * 128 + r, col = kb * kTcBK + c * 8;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < n && col < k) v = *reinterpret_cast<const uint4*>(w + static_cast<size_t>(row) * k + col);
+    out[i] = v;
+  }
+}
+
 template <int BNT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    tc_tile_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
-                   uint16_t* __restrict__ y, int M, int N, int K, int split, int stages) {
+    tc_tile_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, const TcArgs a) {
   constexpr int kBBytes = tc_tile_bbytes(BNT);
   constexpr uint32_t kCols = tc_tile_tmem_cols(BNT);
   constexpr uint32_t kIdesc = umma_idesc_bf16(128, BNT);
   extern __shared__ uint8_t smem_raw[];
+  const int cta = blockIdx.y * gridDim.x + blockIdx.x;
+  const bool tracing = a.trace != nullptr && cta < a.trace_cap && threadIdx.x == 64;  // first epilogue thread
+  const unsigned long long t_start = tracing ? globaltimer() : 0ull;
+  unsigned long long t_ready = 0ull, t_main = 0ull;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stages = a.stages, split = a.split;
   uint8_t* sa = smem;
   uint8_t* sb = smem + static_cast<size_t>(stages) * kTcABytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sb + static_cast<size_t>(stages) * kBBytes);
   uint64_t* empty = full + stages;
   uint64_t* accf = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
   float* part = reinterpret_cast<float*>(smem);  // [BNT][128], reuses the ring after the main loop
 
+  const bool tiles_mode = (a.mode & kTcModeTiles) != 0;
+  const bool global_split = (a.mode & kTcModeGlobalSplit) != 0;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t rank = split > 1 ? cluster_ctarank() : 0u;
+  const uint32_t rank = split == 1 ? 0u : (global_split ? blockIdx.x % split : cluster_ctarank());
   const int rt = blockIdx.x / split;
   const int tt = blockIdx.y;
-  const int nkb = (K + kTcBK - 1) / kTcBK;
+  const int nkb = (a.K + kTcBK - 1) / kTcBK;
   const int kb0 = static_cast<int>(static_cast<long long>(rank) * nkb / split);
   const int kb1 = static_cast<int>(static_cast<long long>(rank + 1) * nkb / split);
   const int nk = kb1 - kb0;
 
   if (threadIdx.x == 0) {
-    prefetch_tensormap(&tmw);
+    if (!tiles_mode) prefetch_tensormap(&tmw);
     prefetch_tensormap(&tmx);
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
@@ -72,24 +119,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (tracing) t_ready = globaltimer();
 
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
-      int issued = 0;
-      for (int i = 0; i < nk; ++i) {
+      const uint8_t* wsrc = a.wtiles + (static_cast<size_t>(rt) * nkb + kb0) * kTcABytes;
+      auto load_w = [&](int i, int s) {
+        if (tiles_mode)
+          bulk_g2s(sa + static_cast<size_t>(s) * kTcABytes, wsrc + static_cast<size_t>(i) * kTcABytes, kTcABytes,
+                   &full[s], pol_w);
+        else
+          tma_load_2d(sa + static_cast<size_t>(s) * kTcABytes, &tmw, &full[s], (kb0 + i) * kTcBK, rt * 128, pol_w);
+      };
+      // Weights never come from the grid this one may overlap with (programmatic launch), so the
+      // first ring-full of W streams before the dependency wait; x only after it.
+      const int pre = min(stages, nk);
+      for (int i = 0; i < pre; ++i) {
+        mbar_expect_tx(&full[i], static_cast<uint32_t>(kTcABytes + kBBytes));
+        load_w(i, i);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(sb + static_cast<size_t>(i) * kBBytes, &tmx, &full[i], (kb0 + i) * kTcBK, tt * BNT, pol_x);
+      int issued = pre;
+      for (int i = pre; i < nk; ++i) {
         const int s = i % stages;
         if (!mbar_wait(&empty[s], ((i / stages) & 1) ^ 1, kErrTcProducer)) break;
         mbar_expect_tx(&full[s], static_cast<uint32_t>(kTcABytes + kBBytes));
-        const int kc = (kb0 + i) * kTcBK;
-        tma_load_2d(sa + static_cast<size_t>(s) * kTcABytes, &tmw, &full[s], kc, rt * 128, pol_w);
-        tma_load_2d(sb + static_cast<size_t>(s) * kBBytes, &tmx, &full[s], kc, tt * BNT, pol_x);
+        load_w(i, s);
+        tma_load_2d(sb + static_cast<size_t>(s) * kBBytes, &tmx, &full[s], (kb0 + i) * kTcBK, tt * BNT, pol_x);
         ++issued;
       }
       for (int i = max(0, issued - stages); i < issued; ++i)
         mbar_wait(&full[i % stages], (i / stages) & 1, kErrDrain, kWaitLimitNs / 10);
     }
+    pdl_launch_dependents();
   } else if (warp == 1) {
     if (lane == 0) {
       for (int i = 0; i < nk; ++i) {
@@ -105,6 +171,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       umma_commit(accf);  // always: also fences any UMMA still in flight on the error path
     }
+    pdl_launch_dependents();
   } else {
     // Epilogue warps 2..5.
     const int q = warp & 3;
@@ -112,6 +179,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int n = rt * 128 + rl;
     const bool ok = __all_sync(0xffffffffu, mbar_wait(accf, 0, kErrTcEpilogue));  // tcgen05.ld is warp-wide
     tc_fence_after();
+    if (tracing) t_main = globaltimer();
+    pdl_launch_dependents();  // with warps 0 and 1 below: this CTA's loads are done, the next grid may start
+    pdl_wait();               // y and the split-K counters may still be in use by the previous grid
+    const int tile_id = rt * gridDim.y + tt;
+    float* gpart = global_split ? a.partials + (static_cast<size_t>(tile_id) * split + rank) * (BNT * 128) : nullptr;
     if (ok) {
 #pragma unroll 1
       for (int c = 0; c < BNT; c += 16) {
@@ -121,29 +193,72 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = tt * BNT + c + j;
-            if (m < M && n < N) y[static_cast<size_t>(m) * N + n] = f32_to_bf16(v[j]);
+            if (m < a.M && n < a.N) a.y[static_cast<size_t>(m) * a.N + n] = f32_to_bf16(v[j]);
           }
+        } else if (global_split) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) __stcg(gpart + (c + j) * 128 + rl, v[j]);
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) part[(c + j) * 128 + rl] = v[j];
         }
       }
     }
+    if (global_split && split > 1) {
+      // Publish this partial, take a ticket; the last of the tile's `split` CTAs reduces.
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (rl == 0) *last_flag = (ticket_acq_rel(a.counters + tile_id) == split - 1) ? 1 : 0;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*last_flag) {
+        const float* base = a.partials + static_cast<size_t>(tile_id) * split * (BNT * 128) + rl;
+        // 16 tokens at a time, up to 8 peers' partials in flight together, added in rank order.
+        for (int c = 0; c < BNT && tt * BNT + c < a.M; c += 16) {
+          float sum[16];
+          sum_partials16(base + c * 128, split, BNT * 128, sum);
+          if (n < a.N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = tt * BNT + c + j;
+              if (m < a.M) a.y[static_cast<size_t>(m) * a.N + n] = f32_to_bf16(sum[j]);
+            }
+          }
+        }
+        if (rl == 0) a.counters[tile_id] = 0;  // leave the counter as the next launch expects it
+      }
+    }
   }
 
-  if (split > 1) {
+  if (split > 1 && !global_split) {
     cluster_sync();  // every peer's partial is in its shared memory
     if (warp >= 2) {
       const int rl = threadIdx.x - 64;
       const int n = rt * 128 + rl;
-      const uint32_t mine = smem_u32(part);
-      for (int j = static_cast<int>(rank); j < BNT; j += split) {
-        const int m = tt * BNT + j;
-        if (m >= M) break;
-        const uint32_t off = static_cast<uint32_t>((j * 128 + rl) * 4);
-        float sum = 0.f;
-        for (int p = 0; p < split; ++p) sum += ld_dsmem_f32(map_peer(mine + off, static_cast<uint32_t>(p)));
-        if (n < N) y[static_cast<size_t>(m) * N + n] = f32_to_bf16(sum);
+      const uint32_t mine = smem_u32(part) + static_cast<uint32_t>(rl * 4);
+      // Tokens r, r + split, ... of this tile: up to 8 at a time, each peer's 8 values in flight
+      // together, peers summed in rank order.
+      for (int j0 = static_cast<int>(rank); j0 < BNT && tt * BNT + j0 < a.M; j0 += 8 * split) {
+        float sum[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) sum[q] = 0.f;
+        for (int p = 0; p < split; ++p) {
+          const uint32_t peer = map_peer(mine, static_cast<uint32_t>(p));
+          float v[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int j = j0 + q * split;
+            v[q] = j < BNT ? ld_dsmem_f32(peer + static_cast<uint32_t>(j * 128 * 4)) : 0.f;
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) sum[q] += v[q];
+        }
+        if (n < a.N) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int j = j0 + q * split;
+            const int m = tt * BNT + j;
+            if (j < BNT && m < a.M) a.y[static_cast<size_t>(m) * a.N + n] = f32_to_bf16(sum[q]);
+          }
+        }
       }
     }
     cluster_sync();  // no CTA leaves while a peer may still read its partial
@@ -155,6 +270,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kCols);
   }
+  if (tracing) a.trace[cta] = TraceRec{t_start, t_ready, t_main, globaltimer(), smid(), static_cast<unsigned>(cta), 0u, 0u};
 }
 
 }  // namespace muse

@@ -35,6 +35,10 @@ from .contract import UNPOOL_SLICE, SLICED_MAX_TOKENS
 from .dispatch import Dispatch
 
 
+# Split-K scratch allocated in prepare (counters + FP32 partials); grown on demand outside capture.
+SCRATCH_BYTES = 8 * 1024 * 1024
+
+
 class Weights(TypedDict):
     qkv_gate: torch.Tensor  # bfloat16 [2304, 8192]
     o: torch.Tensor         # bfloat16 [8192, 1024]
@@ -86,13 +90,14 @@ class _Enc12Device:
 
 
 def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | None = None,
-            self_check: bool = True, verbose: bool = True) -> dict:
+            self_check: bool = True, verbose: bool = True, pdl: bool = True) -> dict:
     """Builds the state kernel_fn serves from. ``weights``: name -> W [N, K] on the GPU (BF16;
     FP32 entries are kept but not served). ``encode_12b`` forces (True) or forbids (False) the
     12-bit copies; None lets the dispatch table decide."""
     _lib.load()
     disp = dispatch if dispatch is not None else Dispatch()
-    state = {"weights": {}, "fp32": {}, "enc12": {}, "dispatch": disp, "checked": []}
+    state = {"weights": {}, "tiles": {}, "fp32": {}, "enc12": {}, "dispatch": disp, "checked": [],
+             "scratch": None, "scratch_need": {}, "pdl": pdl, "pdl_plans": {}}
     for name, w in weights.items():
         if w.dtype != torch.bfloat16:
             state["fp32"][name] = w.contiguous()
@@ -102,6 +107,10 @@ def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | 
         w = w.contiguous()
         state["weights"][name] = w
         n, k = w.shape
+        if k % 8 == 0:  # the tensor-core path streams W from contiguous swizzled 16 KB tiles
+            tiles = torch.empty(_lib.tiles_bytes(n, k), dtype=torch.uint8, device=w.device)
+            _lib.pack_tiles(w.data_ptr(), tiles.data_ptr(), n, k, torch.cuda.current_stream(w.device).cuda_stream)
+            state["tiles"][name] = tiles
         widths = [n] + ([UNPOOL_SLICE] if name == "unpooler" and n > UNPOOL_SLICE else [])
         want = encode_12b if encode_12b is not None else any(disp.wants_12b(nn, k) for nn in widths)
         if want and k % codec12.UNIT == 0 and k <= 65536:
@@ -113,6 +122,8 @@ def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | 
                 state["enc12"][name] = _Enc12Device(enc, w.device)
                 if verbose:
                     print(f"muse: {name}: 12-bit planes, {enc.n_esc} escapes ({enc.escape_fraction:.4%})")
+    state["scratch"] = torch.zeros(SCRATCH_BYTES, dtype=torch.uint8, device=next(iter(state["weights"].values())).device
+                                   if state["weights"] else "cuda")
     if self_check:
         for name, w in state["weights"].items():
             n, k = w.shape
@@ -182,13 +193,43 @@ def project(x: torch.Tensor, state: dict, layer: str, n: int | None = None,
     m = x.shape[0]
     enc = state["enc12"].get(layer)
     plan, fmt = state["dispatch"].plan(m, n, k, enc is not None)
+    if state.get("pdl", True) and not plan.flags & _lib.FLAG_PDL:
+        # The weights are prepare-time constants, so the kernel may stream them before the
+        # previous kernel in the stream has finished (programmatic dependent launch).
+        plan = state["pdl_plans"].setdefault(plan.key(), _lib.MusePlan.from_dict({**plan.as_dict(),
+                                                                                "flags": plan.flags | _lib.FLAG_PDL}))
     y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     stream = torch.cuda.current_stream(x.device).cuda_stream
     if fmt == "12b":
         _lib.proj_12b(enc.view(n), x.data_ptr(), y.data_ptr(), m, plan, stream)
+    elif plan.kernel in _lib.TILE_KERNELS and layer in state["tiles"]:
+        scratch = _scratch_for(state, m, n, k, plan)
+        _lib.proj_bf16_tiles(x.data_ptr(), state["tiles"][layer].data_ptr(), y.data_ptr(), m, n, k, plan, stream,
+                             scratch.data_ptr() if scratch is not None else 0,
+                             scratch.numel() if scratch is not None else 0)
     else:
-        _lib.proj_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, plan, stream)
+        scratch = _scratch_for(state, m, n, k, plan)
+        _lib.proj_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, plan, stream,
+                       scratch.data_ptr() if scratch is not None else 0, scratch.numel() if scratch is not None else 0)
     return y
+
+
+def _scratch_for(state: dict, m: int, n: int, k: int, plan) -> torch.Tensor | None:
+    """The state's zeroed split-K scratch when the plan needs one (grown outside graph capture)."""
+    key = (m, n, k, plan.key())
+    need = state["scratch_need"].get(key)
+    if need is None:
+        need = _lib.scratch_bytes(m, n, k, plan)
+        state["scratch_need"][key] = need
+    if need == 0:
+        return None
+    buf = state["scratch"]
+    if buf is None or buf.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(f"split-K scratch of {need} bytes needed inside graph capture; call once before capturing")
+        buf = torch.zeros(need, dtype=torch.uint8, device=state["scratch"].device if buf is not None else "cuda")
+        state["scratch"] = buf
+    return buf
 
 
 def kernel_fn(data: Inputs, state) -> torch.Tensor:

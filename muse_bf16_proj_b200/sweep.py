@@ -1,0 +1,323 @@
+"""Per-shape plan sweep on a B200: times every candidate plan and writes the dispatch table.
+
+    python -m muse_bf16_proj_b200.sweep [--shapes reference,baseline] [--ms 1,2,...] [--out path]
+                                        [--write-table] [--reps 40]
+
+Replaces the reference's Optuna / grid sweeps (sweep_all.py, sweep_cuda.py) with a plain grid: for
+each (N, K, M) every candidate plan is first checked against a torch FP32 product rounded to BF16
+(TF32 off; relative L2 <= 1e-3), then timed over `reps` launches with CUDA events, each launch on the next
+of R weight copies whose total exceeds the 126 MB L2 (every launch reads W cold from HBM, as the
+reference's judge flushes L2). The fastest checked plan per shape becomes a table row; 12-bit
+candidates are timed too and win a row only when faster than every BF16 plan.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import time
+
+import numpy as np
+import torch
+
+from . import _lib, codec12
+from .contract import BASELINE_LAYERS, LAYERS, UNPOOL_SLICE
+from .dispatch import TABLE_PATH
+
+L2_BYTES = 126 * 1024 * 1024
+
+REFERENCE_SHAPES = [(LAYERS[n][0], LAYERS[n][1]) for n in ("qkv_gate", "o", "pooler", "unpooler")] + [(UNPOOL_SLICE, 4096)]
+BASELINE_SHAPES = [BASELINE_LAYERS[n] for n in ("qkv_decode", "qkv_prefill")]
+DEFAULT_MS = [1, 2, 4, 8, 16, 32, 64, 128, 256]
+
+
+def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[str, _lib.MusePlan]]:
+    """The plans worth timing at this shape: CUDA-core GEMVs at few tokens, the tile kernel with
+    cluster or global split-K, and the stream-K kernel."""
+    out = []
+    if m <= 4 and k % 256 == 0:
+        for warps, ctas in ((16, sms), (16, 2 * sms), (8, 2 * sms)):
+            out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_GEMV_BF16, warps=warps, ctas=ctas, chunk=16)))
+    if twelve_ok and m <= 4:
+        for warps, ctas in ((8, 2 * sms), (16, sms), (16, 2 * sms)):
+            out.append(("12b", _lib.MusePlan(kernel=_lib.KERNEL_GEMV_12B, warps=warps, ctas=ctas)))
+    bnt = 16
+    while bnt < m and bnt < 256:
+        bnt *= 2
+    nkb = (k + 63) // 64
+    tiles = ((n + 127) // 128) * ((m + bnt - 1) // bnt)
+    for split in (1, 2, 3, 4, 6, 8, 12, 16):
+        if split > nkb or (split > 1 and tiles * split > 2 * sms) or (split == 1 and tiles < sms // 2 and nkb > 8):
+            continue
+        if split == 1:
+            out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=bnt, split=1)))
+            continue
+        out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=bnt, split=split,
+                                          flags=_lib.FLAG_GLOBAL_SPLIT)))
+        if split <= 4 and tiles * split <= sms:
+            out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=bnt, split=split)))
+    if bnt <= 128:
+        for stages, ctas in ((4, 2 * sms), (6, sms), (8, sms)):
+            if bnt >= 128 and ctas > sms:
+                continue
+            out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_STREAMK, tile_n=bnt, stages=stages, ctas=ctas)))
+    return out
+
+
+class ShapeBench:
+    """R cold copies of one weight shape (BF16 and, when requested, 12-bit) and their inputs."""
+
+    def __init__(self, n: int, k: int, m_max: int, twelve: bool, seed: int = 0):
+        self.n, self.k = n, k
+        copy_bytes = n * k * 2
+        self.rot = max(2, min(12, math.ceil(3 * L2_BYTES / copy_bytes)))
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        self.w = [(torch.randn((n, k), generator=g, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(self.rot)]
+        self.x = [torch.randn((m_max, k), generator=g, device="cuda").to(torch.bfloat16) for _ in range(self.rot)]
+        self.y = [torch.empty((m_max, n), dtype=torch.bfloat16, device="cuda") for _ in range(self.rot)]
+        st = torch.cuda.current_stream().cuda_stream
+        self.tiles = []
+        for w in self.w:
+            t = torch.empty(_lib.tiles_bytes(n, k), dtype=torch.uint8, device="cuda")
+            _lib.pack_tiles(w.data_ptr(), t.data_ptr(), n, k, st)
+            self.tiles.append(t)
+        self.scratch = torch.zeros(64 << 20, dtype=torch.uint8, device="cuda")
+        self.enc = []
+        if twelve and k % 512 == 0:
+            from .submission import _Enc12Device
+            for w in self.w:
+                host = codec12.encode(w.cpu().view(torch.int16).numpy().view(np.uint16))
+                self.enc.append(_Enc12Device(host, torch.device("cuda")))
+
+    def launch(self, i: int, m: int, fmt: str, plan: _lib.MusePlan) -> None:
+        j = i % self.rot
+        st = torch.cuda.current_stream().cuda_stream
+        if fmt == "12b":
+            _lib.proj_12b(self.enc[j].view(self.n), self.x[j].data_ptr(), self.y[j].data_ptr(), m, plan, st)
+        elif plan.kernel in _lib.TILE_KERNELS:
+            _lib.proj_bf16_tiles(self.x[j].data_ptr(), self.tiles[j].data_ptr(), self.y[j].data_ptr(), m, self.n,
+                                 self.k, plan, st, self.scratch.data_ptr(), self.scratch.numel())
+        else:
+            _lib.proj_bf16(self.x[j].data_ptr(), self.w[j].data_ptr(), self.y[j].data_ptr(), m, self.n, self.k, plan, st)
+
+    def check(self, m: int, fmt: str, plan: _lib.MusePlan) -> float:
+        self.y[0].fill_(float("nan"))
+        self.launch(0, m, fmt, plan)
+        torch.cuda.synchronize()
+        if _lib.device_error(torch.cuda.current_stream().cuda_stream):
+            return float("inf")
+        ref = (self.x[0][:m].float() @ self.w[0].float().T).to(torch.bfloat16).float()
+        got = self.y[0][:m].float()
+        if not torch.isfinite(got).all():
+            return float("inf")
+        return ((got - ref).norm() / ref.norm()).item()
+
+    def time_us(self, m: int, fmt: str, plan: _lib.MusePlan, reps: int) -> tuple[float, float]:
+        """(back-to-back, bracketed) microseconds per launch: `reps` launches timed as one batch
+        (start/end events only; the event clock ticks coarsely, so batches time precisely), and
+        the mean of per-launch event pairs."""
+        for i in range(3):
+            self.launch(i, m, fmt, plan)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(int(4e6 + reps * 1e5))  # host runs ahead of the GPU: no launch gaps
+        start.record()
+        for i in range(reps):
+            self.launch(i, m, fmt, plan)
+        end.record()
+        torch.cuda.synchronize()
+        batch = start.elapsed_time(end) * 1e3 / reps
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        torch.cuda._sleep(int(4e6 + reps * 1e5))
+        for i, (a, b) in enumerate(evs):
+            a.record()
+            self.launch(i, m, fmt, plan)
+            b.record()
+        torch.cuda.synchronize()
+        return batch, statistics.mean(a.elapsed_time(b) * 1e3 for a, b in evs)
+
+
+def trace_plan(sb: "ShapeBench", m: int, fmt: str, plan: _lib.MusePlan, log, launches: int = 4) -> dict:
+    """Runs the plan `launches` times back to back, each launch tracing into its own buffer, and
+    summarises every launch on one clock: first CTA start, last CTA end, per-CTA prologue / main
+    loop / epilogue medians. Consecutive launches overlapping (programmatic launch) shows up as a
+    launch starting before the previous one ended."""
+    cap = 4096
+    bufs = [torch.zeros(cap * _lib.TRACE_RECORD_BYTES // 8, dtype=torch.int64, device="cuda") for _ in range(launches)]
+    for i in range(3):
+        sb.launch(i, m, fmt, plan)
+    torch.cuda.synchronize()
+    try:
+        for i in range(launches):
+            _lib.set_trace(bufs[i].data_ptr(), cap)
+            sb.launch(3 + i, m, fmt, plan)
+    finally:
+        _lib.set_trace(0, 0)
+    torch.cuda.synchronize()
+    per, raws = [], []
+    t_origin = None
+    for b in bufs:
+        rec = b.cpu().numpy().reshape(cap, 6)
+        t = rec[:, :4].astype(np.int64)
+        valid = t[:, 3] > 0
+        t = t[valid]
+        if t_origin is None:
+            t_origin = t[:, 0].min()
+        rel = (t - t_origin) / 1e3
+        per.append({"ctas": int(valid.sum()), "first_start": round(float(rel[:, 0].min()), 3),
+                    "last_start": round(float(rel[:, 0].max()), 3), "first_end": round(float(rel[:, 3].min()), 3),
+                    "last_end": round(float(rel[:, 3].max()), 3),
+                    "prologue": round(float(np.median(rel[:, 1] - rel[:, 0])), 3),
+                    "main_med": round(float(np.median(rel[:, 2] - rel[:, 1])), 3),
+                    "main_max": round(float(np.max(rel[:, 2] - rel[:, 1])), 3),
+                    "tail_med": round(float(np.median(rel[:, 3] - rel[:, 2])), 3),
+                    "tail_max": round(float(np.max(rel[:, 3] - rel[:, 2])), 3)})
+        meta = rec[valid, 4].astype(np.uint64)
+        raws.append({"t_us": rel.round(3).tolist(), "sm": (meta & 0xFFFFFFFF).astype(np.int64).tolist(),
+                     "cta": ((meta >> 32) & 0xFFFFFFFF).astype(np.int64).tolist()})
+    for i, p in enumerate(per):
+        log(f"trace n={sb.n} k={sb.k} m={m} {plan.as_dict()['kernel']} flags={plan.flags} launch {i}: {json.dumps(p)}")
+    return {"launches": per, "raw": raws}
+
+
+def sweep_shape(n, k, ms, reps, sms, twelve, log, only=None, trace=False, extra_flags=0):
+    sb = ShapeBench(n, k, max(ms), twelve)
+    rows = []
+    for m in ms:
+        results = []
+        cands = only if only is not None else candidates(m, n, k, sms, twelve and bool(sb.enc))
+        if extra_flags:
+            cands = [(f, _lib.MusePlan.from_dict({**p.as_dict(), "flags": p.flags | extra_flags})) for f, p in cands]
+        for fmt, plan in cands:
+            try:
+                err = sb.check(m, fmt, plan)
+            except _lib.MuseError as e:
+                log(f"  n={n} k={k} m={m} {fmt} {plan.as_dict()}: {e}")
+                continue
+            if not err <= 1e-3:
+                log(f"  n={n} k={k} m={m} {fmt} {plan.as_dict()}: WRONG rel {err:.3e}")
+                continue
+            med, mean = sb.time_us(m, fmt, plan, reps)
+            tr = trace_plan(sb, m, fmt, plan, log) if trace else None
+            wbytes = n * k * (1.5 if fmt == "12b" else 2)
+            gbs = (wbytes + m * k * 2 + m * n * 2) / (med * 1e-6) / 1e9
+            results.append({"fmt": fmt, "plan": plan.as_dict(), "us": med, "us_mean": mean, "gbs": gbs, "rel": err,
+                            "trace": tr})
+        results.sort(key=lambda r: r["us"])
+        best16 = next((r for r in results if r["fmt"] == "bf16"), None)
+        for r in results[:3]:
+            log(f"n={n} k={k} m={m}: {r['us']:.2f} us {r['gbs']:.0f} GB/s {r['fmt']} {r['plan']}")
+        rows.append({"n": n, "k": k, "m": m, "best": results[0] if results else None, "best_bf16": best16,
+                     "all": results})
+    del sb
+    torch.cuda.empty_cache()
+    return rows
+
+
+def table_entries(rows) -> list[dict]:
+    """Dispatch rows from sweep results. The winner timed at M serves (previous timed M, M];
+    neighbouring ranges with the same plan merge. Where the overall winner is 12-bit, the best
+    BF16 plan gets a row too, for layers served without 12-bit planes. 12-bit rows come first."""
+    by_shape: dict = {}
+    for r in rows:
+        by_shape.setdefault((r["n"], r["k"]), []).append(r)
+    entries = []
+    for (n, k), rs in sorted(by_shape.items()):
+        rs.sort(key=lambda r: r["m"])
+        for key in ("best", "best_bf16"):
+            cur, prev_m = None, 0
+            for r in rs:
+                lo, hi, prev_m = prev_m + 1, r["m"], r["m"]
+                b = r[key]
+                if b is None or (key == "best_bf16" and r["best"] is not None and r["best"]["fmt"] == "bf16"):
+                    cur = None
+                    continue
+                plan = {kk: v for kk, v in b["plan"].items() if v}
+                if cur is not None and cur["plan"] == plan and cur["weights"] == b["fmt"] and cur["m_hi"] == lo - 1:
+                    cur["m_hi"] = hi
+                    cur["us"][str(r["m"])] = round(b["us"], 3)
+                    continue
+                cur = {"n": n, "k": k, "m_lo": lo, "m_hi": hi, "weights": b["fmt"], "plan": plan,
+                       "us": {str(r["m"]): round(b["us"], 3)}}
+                entries.append(cur)
+    entries.sort(key=lambda e: (e["n"], e["k"], 0 if e["weights"] == "12b" else 1, e["m_lo"]))
+    merged = []
+    for e in entries:
+        p = merged[-1] if merged else None
+        if (p is not None and (p["n"], p["k"], p["weights"]) == (e["n"], e["k"], e["weights"])
+                and p["plan"] == e["plan"] and p["m_hi"] + 1 == e["m_lo"]):
+            p["m_hi"] = e["m_hi"]
+            p["us"].update(e["us"])
+        else:
+            merged.append(e)
+    return merged
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--shapes", default="reference,baseline")
+    ap.add_argument("--ms", default=",".join(map(str, DEFAULT_MS)))
+    ap.add_argument("--reps", type=int, default=40)
+    ap.add_argument("--no-12b", action="store_true")
+    ap.add_argument("--out", default="gpurun_out/sweep.json")
+    ap.add_argument("--write-table", action="store_true")
+    ap.add_argument("--plan", default="", help='time only this plan, e.g. {"kernel": "tc_tile", "split": 3}')
+    ap.add_argument("--trace", action="store_true", help="also record per-CTA timestamps of each plan")
+    ap.add_argument("--flags", type=int, default=0, help="plan flags OR-ed into every candidate (2 = PDL)")
+    ap.add_argument("--from-json", default="", help="write the table from an earlier sweep's JSON (no GPU)")
+    args = ap.parse_args()
+    if args.from_json:
+        with open(args.from_json) as f:
+            done = json.load(f)
+        write_table(done["rows"], done.get("device", "?"), print)
+        return
+    torch.backends.cuda.matmul.allow_tf32 = False
+    only = None
+    if args.plan:
+        d = json.loads(args.plan)
+        only = [("12b" if d.get("kernel") == "gemv_12b" else "bf16", _lib.MusePlan.from_dict(d))]
+    shapes = []
+    for s in args.shapes.split(","):
+        if s == "reference":
+            shapes += REFERENCE_SHAPES
+        elif s == "baseline":
+            shapes += BASELINE_SHAPES
+        elif "x" in s:
+            a, b = s.split("x")
+            shapes.append((int(a), int(b)))
+    ms = [int(v) for v in args.ms.split(",")]
+    sms = _lib.sm_count()
+    lines = []
+
+    def log(msg):
+        print(msg, flush=True)
+        lines.append(msg)
+
+    t0 = time.time()
+    rows = []
+    for n, k in shapes:
+        shape_ms = [m for m in ms if not (n == UNPOOL_SLICE and m > 8)]
+        rows += sweep_shape(n, k, shape_ms, args.reps, sms, not args.no_12b, log, only, args.trace, args.flags)
+    os.makedirs(os.path.dirname(args.out) or ".", exist_ok=True)
+    with open(args.out, "w") as f:
+        json.dump({"device": torch.cuda.get_device_name(), "sms": sms, "rows": rows,
+                   "seconds": time.time() - t0}, f)
+    if args.write_table:
+        write_table(rows, torch.cuda.get_device_name(), log)
+
+
+def write_table(rows, device: str, log) -> None:
+    table = {"generated_by": "python -m muse_bf16_proj_b200.sweep --write-table (or --from-json of its output)",
+             "device": device,
+             "timing": "us = mean per launch of 30 back-to-back launches (programmatic launch), weights cold in L2",
+             "entries": table_entries(rows)}
+    with open(TABLE_PATH, "w") as f:
+        json.dump(table, f, indent=1)
+    log(f"wrote {len(table['entries'])} rows to {TABLE_PATH}")
+
+
+if __name__ == "__main__":
+    main()

@@ -26,11 +26,17 @@ def test_proj_argument_errors_before_any_device_work():
     lib = _lib.load()
     plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, split=1, tile_n=16)
     p = ctypes.byref(plan)
-    assert lib.muse_proj_bf16(None, 16, 16, 1, 128, 64, p, None) == -1
-    assert lib.muse_proj_bf16(16, 16, 16, 0, 128, 64, p, None) == -1
-    assert lib.muse_proj_bf16(18, 16, 16, 1, 128, 64, p, None) == -2   # x misaligned
-    assert lib.muse_proj_bf16(16, 16, 16, 1, 128, 60, p, None) == -2   # K * 2 not a multiple of 16
-    assert lib.muse_proj_bf16(16, 16, 16, 1, 128, 64, None, None) == -1
+    assert lib.muse_proj_bf16(None, 16, 16, 1, 128, 64, p, None, 0, None) == -1
+    assert lib.muse_proj_bf16(16, 16, 16, 0, 128, 64, p, None, 0, None) == -1
+    assert lib.muse_proj_bf16(18, 16, 16, 1, 128, 64, p, None, 0, None) == -2   # x misaligned
+    assert lib.muse_proj_bf16(16, 16, 16, 1, 128, 60, p, None, 0, None) == -2   # K * 2 not a multiple of 16
+    assert lib.muse_proj_bf16(16, 16, 16, 1, 128, 64, None, None, 0, None) == -1
+    assert lib.muse_proj_bf16_tiles(None, 16, 16, 1, 128, 64, p, None, 0, None) == -1
+    assert lib.muse_proj_bf16_tiles(16, 16, 16, 1, 128, 64, ctypes.byref(_lib.MusePlan(kernel=1)), None, 0, None) == -7
+    assert lib.muse_pack_tiles(None, 16, 128, 64, None) == -1
+    assert lib.muse_pack_tiles(16, 16, 128, 60, None) == -2
+    b = ctypes.c_int64()
+    assert lib.muse_tiles_bytes(200, 200, ctypes.byref(b)) == 0 and b.value == 2 * 4 * 16384
     enc = _lib.MuseEnc12(16, 16, 16, 16, 128, 512, 0)
     plan12 = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE)
     assert lib.muse_proj_12b(ctypes.byref(enc), 16, 16, 1, ctypes.byref(plan12), None) == -7

@@ -83,12 +83,27 @@ def _rand_bits(shape, seed, scale=1.0):
     return bits((torch.randn(shape, generator=g) * scale).to(torch.bfloat16))
 
 
-def _run_bf16(x_bits, w_bits, plan, n=None):
+_SCRATCH = {}
+
+
+def scratch_buf():
+    if "buf" not in _SCRATCH:
+        _SCRATCH["buf"] = torch.zeros(32 << 20, dtype=torch.uint8, device="cuda")
+    return _SCRATCH["buf"]
+
+
+def _run_bf16(x_bits, w_bits, plan, n=None, tiles=False):
     x, w = to_dev(x_bits), to_dev(w_bits)
     m, k = x.shape
     n = w.shape[0] if n is None else n
     y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
-    _lib.proj_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, plan, stream())
+    sc = scratch_buf()
+    if tiles:
+        t = torch.empty(_lib.tiles_bytes(w.shape[0], k), dtype=torch.uint8, device="cuda")
+        _lib.pack_tiles(w.data_ptr(), t.data_ptr(), w.shape[0], k, stream())
+        _lib.proj_bf16_tiles(x.data_ptr(), t.data_ptr(), y.data_ptr(), m, n, k, plan, stream(), sc.data_ptr(), sc.numel())
+    else:
+        _lib.proj_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, plan, stream(), sc.data_ptr(), sc.numel())
     return y
 
 
@@ -125,14 +140,47 @@ TC_CASES = [  # (m, n, k, tile_n, split)
 ]
 
 
+@pytest.mark.parametrize("variant", ["rowmajor", "tiles", "tiles_global"])
 @pytest.mark.parametrize("m,n,k,tile_n,split", TC_CASES)
-def test_tc_tile(m, n, k, tile_n, split):
+def test_tc_tile(m, n, k, tile_n, split, variant):
     xb, wb = _rand_bits((m, k), 10 + m), _rand_bits((n, k), 20 + n, 0.02)
-    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=tile_n, split=split)
-    y = _run_bf16(xb, wb, plan)
-    assert_parity(xb, wb, y, what=f"tc m={m} n={n} k={k} tile={tile_n} split={split}")
-    y2 = _run_bf16(xb, wb, plan)
+    flags = _lib.FLAG_GLOBAL_SPLIT if variant == "tiles_global" else 0
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=tile_n, split=split, flags=flags)
+    tiles = variant != "rowmajor"
+    y = _run_bf16(xb, wb, plan, tiles=tiles)
+    assert_parity(xb, wb, y, what=f"tc {variant} m={m} n={n} k={k} tile={tile_n} split={split}")
+    y2 = _run_bf16(xb, wb, plan, tiles=tiles)
     assert torch.equal(y.view(torch.int16), y2.view(torch.int16)), "split-K reduction is not deterministic"
+    if flags:
+        assert int(torch.count_nonzero(scratch_buf()[: 64 * 1024])) == 0, "split-K counters not back at 0"
+
+
+def test_tc_tile_global_split_large_splits():
+    m, n, k = 16, 1024, 8192
+    xb, wb = _rand_bits((m, k), 41), _rand_bits((n, k), 42, 0.02)
+    for split in (20, 32, 64):
+        plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=16, split=split, flags=_lib.FLAG_GLOBAL_SPLIT)
+        assert_parity(xb, wb, _run_bf16(xb, wb, plan, tiles=True), what=f"tc global split={split}")
+    assert int(torch.count_nonzero(scratch_buf()[: 64 * 1024])) == 0
+
+
+def test_pack_tiles_layout():
+    """The packed copy holds exactly W's values: row r, 16-byte chunk c at position c ^ (r % 8)."""
+    n, k = 200, 200
+    wb = _rand_bits((n, k), 55)
+    w = to_dev(wb)
+    t = torch.empty(_lib.tiles_bytes(n, k), dtype=torch.uint8, device="cuda")
+    _lib.pack_tiles(w.data_ptr(), t.data_ptr(), n, k, stream())
+    torch.cuda.synchronize()
+    tb = t.cpu().numpy().view(np.uint16).reshape(2, 4, 128, 8, 8)  # [rt][kb][r][chunk pos][8]
+    expect = np.zeros((256, 256), dtype=np.uint16)
+    expect[:n, :k] = wb
+    for rt in range(2):
+        for kb in range(4):
+            for r in range(128):
+                for c in range(8):
+                    got = tb[rt, kb, r, c ^ (r % 8)]
+                    assert np.array_equal(got, expect[rt * 128 + r, kb * 64 + c * 8: kb * 64 + c * 8 + 8])
 
 
 def test_tc_tile_stage_counts():
@@ -151,7 +199,7 @@ def test_plan_errors_on_device():
            _lib.MusePlan(kernel=_lib.KERNEL_GEMV_BF16, warps=5), _lib.MusePlan(kernel=9)]
     for plan in bad:
         with pytest.raises(_lib.MuseError):
-            _lib.proj_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), 4, 256, 4096, plan, stream())
+            _lib.proj_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), 4, 256, 4096, plan, stream(), 0, 0)
     with pytest.raises(_lib.MuseError):  # GEMV needs M <= 8
         x9 = torch.zeros((9, 4096), dtype=torch.bfloat16, device="cuda")
         _lib.proj_bf16(x9.data_ptr(), w.data_ptr(), y.data_ptr(), 9, 256, 4096,
@@ -230,3 +278,74 @@ def test_cuda_graph_replay_with_fresh_inputs(state, ref_weights):
             assert_parity(bits(fresh["x"]), bits(ref_weights[layer]), out, fresh["config"]["n"],
                           what=f"graph {layer} m={m}")
         del g
+
+
+@pytest.mark.parametrize("plan_dict", [
+    {"kernel": "tc_streamk", "tile_n": 16, "stages": 4, "flags": 2},
+    {"kernel": "tc_streamk", "tile_n": 32, "ctas": 37, "flags": 2},
+    {"kernel": "tc_tile", "tile_n": 16, "split": 4, "flags": 1 | 2},
+    {"kernel": "tc_tile", "tile_n": 32, "split": 1, "flags": 2},
+    {"kernel": "gemv_bf16", "warps": 8, "flags": 2},
+])
+def test_programmatic_launch_chain(plan_dict):
+    """Each projection feeds the next (square W): with programmatic launch a kernel must still read
+    the previous kernel's finished output. Same bits as the plain launches."""
+    n = k = 1024
+    m = 8 if plan_dict["kernel"] == "gemv_bf16" else 16
+    wb = _rand_bits((n, k), 61, 1.0 / 32)
+    w = to_dev(wb)
+    t = torch.empty(_lib.tiles_bytes(n, k), dtype=torch.uint8, device="cuda")
+    _lib.pack_tiles(w.data_ptr(), t.data_ptr(), n, k, stream())
+    x0 = to_dev(_rand_bits((m, k), 62))
+    sc = scratch_buf()
+
+    def chain(flags):
+        plan = _lib.MusePlan.from_dict({**plan_dict, "flags": flags})
+        bufs = [x0] + [torch.empty((m, n), dtype=torch.bfloat16, device="cuda") for _ in range(6)]
+        for i in range(6):
+            if plan.kernel in _lib.TILE_KERNELS:
+                _lib.proj_bf16_tiles(bufs[i].data_ptr(), t.data_ptr(), bufs[i + 1].data_ptr(), m, n, k, plan, stream(),
+                                     sc.data_ptr(), sc.numel())
+            else:
+                _lib.proj_bf16(bufs[i].data_ptr(), w.data_ptr(), bufs[i + 1].data_ptr(), m, n, k, plan, stream(),
+                               sc.data_ptr(), sc.numel())
+        torch.cuda.synchronize()
+        assert _lib.device_error(stream()) == 0
+        return [bits(b) for b in bufs[1:]]
+
+    plain = chain(plan_dict["flags"] & ~2)
+    pdl = chain(plan_dict["flags"])
+    for a, b in zip(plain, pdl):
+        assert np.array_equal(a, b)
+    assert_parity(bits(x0), wb, to_dev(plain[0]), what="chain step 1")
+
+
+SK_CASES = [  # (m, n, k, tile_n, stages, ctas)
+    (16, 6144, 4096, 16, 6, 0), (1, 6144, 4096, 16, 4, 0), (16, 6144, 4096, 32, 8, 296),
+    (8, 2304, 8192, 16, 6, 148), (5, 1024, 4096, 16, 6, 0), (32, 4096, 8192, 32, 6, 0),
+    (33, 8192, 1024, 64, 4, 0), (64, 640, 2048, 64, 6, 7), (100, 1000, 1000, 32, 3, 50),
+    (130, 384, 512, 128, 4, 0), (256, 2304, 8192, 128, 4, 0), (7, 10240, 8192, 16, 6, 0),
+    (16, 128, 64, 16, 2, 0), (3, 200, 4096, 16, 5, 1000),
+]
+
+
+@pytest.mark.parametrize("m,n,k,tile_n,stages,ctas", SK_CASES)
+def test_tc_streamk(m, n, k, tile_n, stages, ctas):
+    xb, wb = _rand_bits((m, k), 70 + m), _rand_bits((n, k), 80 + n, 0.02)
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_STREAMK, tile_n=tile_n, stages=stages, ctas=ctas)
+    assert _lib.scratch_bytes(m, n, k, plan) <= scratch_buf().numel()
+    y = _run_bf16(xb, wb, plan, tiles=True)
+    assert_parity(xb, wb, y, what=f"streamk m={m} n={n} k={k} tile={tile_n} stages={stages} ctas={ctas}")
+    y2 = _run_bf16(xb, wb, plan, tiles=True)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16)), "stream-K reduction is not deterministic"
+    assert int(torch.count_nonzero(scratch_buf()[: 64 * 1024])) == 0, "stream-K counters not back at 0"
+
+
+def test_tc_streamk_needs_scratch():
+    x = torch.zeros((4, 1024), dtype=torch.bfloat16, device="cuda")
+    t = torch.zeros(_lib.tiles_bytes(256, 1024), dtype=torch.uint8, device="cuda")
+    y = torch.zeros((4, 256), dtype=torch.bfloat16, device="cuda")
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_STREAMK)
+    with pytest.raises(_lib.MuseError) as e:
+        _lib.proj_bf16_tiles(x.data_ptr(), t.data_ptr(), y.data_ptr(), 4, 256, 1024, plan, stream(), 0, 0)
+    assert e.value.code == -4
