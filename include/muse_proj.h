@@ -142,6 +142,27 @@ int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stre
 int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
                          const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream);
 
+/* Size of the library's built-in scratch area used by muse_proj_bf16_tiles_noalloc. */
+#define MUSE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+
+/*
+ * No counterpart in the reference: an addition for callers that cannot allocate device memory,
+ * such as an inference engine's plugin that is handed only its input and output buffers from the
+ * engine's own pool, or an application whose device memory is budgeted once at start-up.
+ *
+ * Same result as muse_proj_bf16_tiles with a MUSE_KERNEL_TC_STREAMK plan, but the split-K scratch
+ * is a fixed area of MUSE_NOALLOC_SCRATCH_BYTES inside the library (a device variable held by
+ * every GPU that loads the library until the process exits) instead of a caller buffer; the call
+ * itself allocates nothing. Shapes whose scratch need (muse_scratch_bytes) exceeds that size are
+ * rejected with MUSE_ERR_CAPACITY. The first call on each device looks up the area's address
+ * (once per device, with that device current); make that first call before any stream capture.
+ * Every call shares the one area and clears the split-K counters it uses on `stream` before its
+ * launch, so calls whose execution overlaps on the GPU (other streams, other threads) race and
+ * must be serialized by the caller.
+ */
+int muse_proj_bf16_tiles_noalloc(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
+                                 const MusePlan* plan, void* stream);
+
 /*
  * y = x . decode12(W)^T from the 12-bit planes. Replaces nf12_cuda_gemv / nf12_gemv
  * (submission.py:660-673, 357-474). plan->kernel must be MUSE_KERNEL_GEMV_12B; M <= 8.

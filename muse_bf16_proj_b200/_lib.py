@@ -75,6 +75,7 @@ _SIGNATURES = {
     "muse_pack_tiles": ([_P, _P, _I64, _I64, _P], _I32),
     "muse_proj_bf16_tiles": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
     "muse_proj_12b": ([ctypes.POINTER(MuseEnc12), _P, _P, _I64, ctypes.POINTER(MusePlan), _P], _I32),
+    "muse_proj_bf16_tiles_noalloc": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P], _I32),
     "muse_encode12_sizes": ([_I64, _I64, ctypes.POINTER(_I64), ctypes.POINTER(_I64)], _I32),
     "muse_encode12": ([_P, _I64, _I64, _P, _P, _P, _P, _I64, ctypes.POINTER(_I64), _I32], _I32),
     "muse_decode12": ([_P, _P, _P, _P, _I64, _I64, _P, _I32], _I32),
@@ -172,3 +173,14 @@ TRACE_RECORD_BYTES = 48
 def set_trace(ptr: int, capacity: int) -> None:
     """Per-CTA timestamps for later launches into a device buffer (ptr 0 turns tracing off)."""
     check(load().muse_set_trace(ptr or None, capacity))
+
+
+NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024
+
+
+def proj_bf16_tiles_noalloc(x_ptr: int, tiles_ptr: int, y_ptr: int, m: int, n: int, k: int, plan: MusePlan,
+                            stream: int) -> None:
+    """muse_proj_bf16_tiles_noalloc: the stream-K projection with the library's built-in scratch
+    (for callers that cannot allocate device memory); see include/muse_proj.h."""
+    check(load().muse_proj_bf16_tiles_noalloc(x_ptr, tiles_ptr, y_ptr, m, n, k, ctypes.byref(plan),
+                                              ctypes.c_void_p(stream)))

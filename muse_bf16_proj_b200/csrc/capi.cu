@@ -623,3 +623,66 @@ int muse_proj_12b(const MuseEnc12* enc, const void* x, void* y, int64_t m, const
 }
 
 }  // extern "C"
+
+// ---- no-allocation entry point ----------------------------------------------------------------
+//
+// For callers that cannot allocate device memory themselves (an inference engine's plugin that is
+// handed only its input and output buffers from the engine's own pool, or an application whose
+// device memory budget is fixed when it starts): the stream-K projection with its split-K scratch
+// in a fixed-size array inside this library instead of a caller buffer. The array is a
+// file-scope device variable, so every GPU that loads the library holds its
+// MUSE_NOALLOC_SCRATCH_BYTES until the process exits; nothing is allocated per call.
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MUSE_NOALLOC_SCRATCH_BYTES];
+
+void* g_noalloc_addr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// The array's device address on the current device. In host code `g_noalloc_scratch` is only a
+// host-side stand-in for the symbol, so the address is looked up once per device, with that
+// device current, and cached.
+int noalloc_scratch(void** out) {
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(MUSE_ERR_CUDA, "proj_bf16_tiles_noalloc: cudaGetSymbolAddress: %s",
+                  e != cudaSuccess ? cudaGetErrorString(e) : "null address");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return MUSE_OK;
+}
+
+}  // namespace
+
+extern "C" int muse_proj_bf16_tiles_noalloc(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
+                                            const MusePlan* plan, void* stream) {
+  muse::clear_error();
+  if (!x || !tiles || !y || !plan) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles_noalloc: null pointer");
+  if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles_noalloc: non-positive size");
+  if (!aligned16(x) || !aligned16(tiles) || (reinterpret_cast<uintptr_t>(y) & 1u) || (k * 2) % 16)
+    return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles_noalloc: x and tiles 16-byte aligned, y 2-byte aligned, K % 8 == 0");
+  if (plan->kernel != MUSE_KERNEL_TC_STREAMK)
+    return fail(MUSE_ERR_PLAN, "proj_bf16_tiles_noalloc: plan kernel must be TC_STREAMK");
+  SkShape sh;
+  if (int rc = sk_shape(m, n, k, *plan, &sh)) return rc;
+  if (sh.scratch > MUSE_NOALLOC_SCRATCH_BYTES)
+    return fail(MUSE_ERR_CAPACITY,
+                "proj_bf16_tiles_noalloc: this shape and plan need %lld bytes of split-K scratch, the built-in area "
+                "holds %lld (use muse_proj_bf16_tiles with caller scratch, fewer CTAs or a smaller tile_n)",
+                (long long)sh.scratch, (long long)MUSE_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // The array keeps the previous call's contents: the tile counters this call uses must start at 0.
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(sh.tiles) * sizeof(int),
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "proj_bf16_tiles_noalloc: cudaMemsetAsync: %s", cudaGetErrorString(e));
+  return run_streamk(x, tiles, y, m, n, k, *plan, scratch, MUSE_NOALLOC_SCRATCH_BYTES,
+                     static_cast<cudaStream_t>(stream));
+}
