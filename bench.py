@@ -63,6 +63,7 @@ def parse_args():
     ap.add_argument("--gather", action="store_true", help="sharded workloads: also all-gather y (NCCL)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--plan", default="", help="JSON plan overriding the dispatch table for this workload")
     return ap.parse_args()
 
 
@@ -244,6 +245,8 @@ def main():
     entries = None
     if fmt == "12b":
         entries = [{"n": n, "k": k, "m_lo": 1, "m_hi": 8, "weights": "12b", "plan": {"kernel": "gemv_12b"}}]
+    if args.plan:
+        entries = [{"n": n, "k": k, "m_lo": m, "m_hi": m, "weights": fmt, "plan": json.loads(args.plan)}]
     disp = Dispatch(entries=entries) if entries is not None else Dispatch()
     state = submission.prepare(weights, dispatch=disp, encode_12b=(fmt == "12b"), verbose=False)
     names = list(weights)
@@ -336,10 +339,15 @@ def main():
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "algorithmic_bytes_per_launch": int(bytes_step)}
     else:
+        # Back-to-back steps keep the GPU under sustained load (power cap): the sustained GEMM
+        # figure is the denominator; the isolated single launch is held against the burst one.
         achieved = flops_step / (mean_launch_ms * 1e-3) / 1e12
-        peak = peaks["bf16_tflops"]
+        peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        burst = flops_step / (isolated_us * 1e-6) / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "algorithmic_flops_per_launch": flops_step}
+                "frac": round(achieved / peak, 4), "algorithmic_flops_per_launch": flops_step,
+                "peak_kind": "sustained (bf16_tflops_sustained)",
+                "isolated_achieved": round(burst, 1), "isolated_frac_of_burst": round(burst / peaks["bf16_tflops"], 4)}
     roof["peak_source"] = f"{peaks_kind} (MEASURED_PEAKS.json)" if peaks_kind == "measured" else "fallback"
     roof["kernel"] = kernel_name
     roof["mean_launch_us"] = round(mean_launch_ms * 1e3, 3)

@@ -35,6 +35,8 @@ extern "C" {
 #define MUSE_KERNEL_GEMV_12B 2  /* streaming CUDA-core GEMV, 12-bit W, M <= 8 */
 #define MUSE_KERNEL_TC_TILE 3   /* tcgen05 128 x tile_n tiles, K split across a cluster or through scratch */
 #define MUSE_KERNEL_TC_STREAMK 4 /* tcgen05 stream-K over packed tiles: equal work per CTA, one wave */
+#define MUSE_KERNEL_TC_GEMM 5    /* persistent tcgen05 GEMM, 128 tokens x 256 W rows a tile (prefill) */
+#define MUSE_KERNEL_TC_GEMM2 6   /* persistent tcgen05 GEMM on CTA pairs (cta_group::2), 256 x 256 a tile */
 
 /* Plan flags. */
 #define MUSE_FLAG_GLOBAL_SPLIT 1 /* TC_TILE: reduce K-split partials through caller scratch instead of a cluster */
@@ -133,8 +135,10 @@ int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stre
 
 /*
  * y = x . W^T with W given as packed tiles (muse_pack_tiles of the full W: the first
- * ceil(n / 128) row tiles serve W[:n]). plan->kernel: MUSE_KERNEL_TC_TILE or
- * MUSE_KERNEL_TC_STREAMK (which always needs scratch, see muse_scratch_bytes). Each pipeline
+ * ceil(n / 128) row tiles serve W[:n]). plan->kernel: MUSE_KERNEL_TC_TILE,
+ * MUSE_KERNEL_TC_STREAMK (which always needs scratch, see muse_scratch_bytes) or
+ * MUSE_KERNEL_TC_GEMM / MUSE_KERNEL_TC_GEMM2 (prefill; replace the cuBLAS F.linear that served
+ * the reference's large shapes, submission.py:1170). Each pipeline
  * stage moves one contiguous 16 KB tile with a 1-D bulk copy. Replaces TmaGemm.__call__
  * (submission.py:977-988), which read its pre-swizzled W the same way, and the Triton split-K
  * bf16_gemm with its atomic tile tickets (submission.py:209-251, 1084-1107).

@@ -16,10 +16,10 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 
 MUSE_OK = 0
 ERRORS = {-1: "INVALID", -2: "ALIGN", -3: "SHAPE", -4: "CAPACITY", -5: "CUDA", -6: "TIMEOUT", -7: "PLAN"}
-KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE, KERNEL_TC_STREAMK = 1, 2, 3, 4
+KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_GEMM, KERNEL_TC_GEMM2 = 1, 2, 3, 4, 5, 6
 KERNEL_NAMES = {KERNEL_GEMV_BF16: "gemv_bf16", KERNEL_GEMV_12B: "gemv_12b", KERNEL_TC_TILE: "tc_tile",
-                KERNEL_TC_STREAMK: "tc_streamk"}
-TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK)
+                KERNEL_TC_STREAMK: "tc_streamk", KERNEL_TC_GEMM: "tc_gemm", KERNEL_TC_GEMM2: "tc_gemm2"}
+TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_GEMM, KERNEL_TC_GEMM2)
 KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
 FLAG_GLOBAL_SPLIT = 1
 FLAG_PDL = 2

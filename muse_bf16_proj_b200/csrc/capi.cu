@@ -16,6 +16,8 @@
 #include "gemv.cuh"
 #include "tc_tile.cuh"
 #include "tc_streamk.cuh"
+#include "tc_gemm.cuh"
+#include "tc_gemm2.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -75,7 +77,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D BF16 tensor map over a row-major [rows, cols] matrix; box = 64 columns x box_rows rows,
 // 128-byte swizzle; rows and columns past the edge read as zero.
-int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows) {
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
+             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (!fn) return fail(MUSE_ERR_CUDA, "cuTensorMapEncodeTiled entry point not found");
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
@@ -83,7 +86,7 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int
   cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MUSE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return MUSE_OK;
@@ -451,6 +454,127 @@ int run_streamk(const void* x, const void* tiles, void* y, int64_t m, int64_t n,
   }
 }
 
+// ---- persistent prefill GEMM -------------------------------------------------------------------
+
+int run_gemm(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p,
+             cudaStream_t st) {
+  DeviceInfo* d;
+  if (int rc = device_info(&d)) return rc;
+  if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "tc_gemm: dimension too large");
+  const int limit = std::min(kSmemLimit, d->smem_optin);
+  const int max_stages = (limit - 1024 - 128) / (muse::kGmABytes + muse::kGmBBytes + 16);
+  const int stages = p.stages > 0 ? p.stages : std::min(4, max_stages);
+  if (stages < 2 || stages > max_stages) return fail(MUSE_ERR_PLAN, "tc_gemm: %d stages do not fit (max %d)", stages, max_stages);
+  CUtensorMap tmx;
+  if (int rc = make_map(&tmx, x, m, k, 128)) return rc;
+  muse::GmArgs a;
+  a.wtiles = static_cast<const uint8_t*>(tiles);
+  a.y = static_cast<uint16_t*>(y);
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.K = static_cast<int>(k);
+  a.stages = stages;
+  a.mtiles = static_cast<int>((m + 127) / 128);
+  a.ntiles = static_cast<int>((n + muse::kGmBN - 1) / muse::kGmBN);
+  a.nkb = static_cast<int>((k + 63) / 64);
+  a.rtiles = static_cast<int>((n + 127) / 128);
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  const long long tiles_total = static_cast<long long>(a.mtiles) * a.ntiles;
+  if (tiles_total > INT32_MAX) return fail(MUSE_ERR_SHAPE, "tc_gemm: too many tiles");
+  const int grid = static_cast<int>(std::min<long long>(p.ctas > 0 ? p.ctas : d->sms, tiles_total));
+  auto kern = muse::tc_gemm_kernel;
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_gemm): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(muse::kGmThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(muse::gm_smem(stages));
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = (p.flags & MUSE_FLAG_PDL) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmx, a);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_gemm launch: %s", cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
+// ---- persistent prefill GEMM over CTA pairs --------------------------------------------------
+
+int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p,
+              cudaStream_t st) {
+  DeviceInfo* d;
+  if (int rc = device_info(&d)) return rc;
+  if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "tc_gemm2: dimension too large");
+  const int limit = std::min(kSmemLimit, d->smem_optin);
+  const int max_stages = (limit - 1024 - 128) / (muse::kG2Stage + 16);
+  const int stages = p.stages > 0 ? p.stages : std::min(6, max_stages);
+  if (stages < 2 || stages > max_stages) return fail(MUSE_ERR_PLAN, "tc_gemm2: %d stages do not fit (max %d)", stages, max_stages);
+  muse::G2Args a;
+  a.y = static_cast<uint16_t*>(y);
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.K = static_cast<int>(k);
+  a.stages = stages;
+  a.mtiles = static_cast<int>((m + 255) / 256);
+  a.ntiles = static_cast<int>((n + 255) / 256);
+  a.nkb = static_cast<int>((k + 63) / 64);
+  a.rtiles = static_cast<int>((n + 127) / 128);
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  const long long tiles_total = static_cast<long long>(a.mtiles) * a.ntiles;
+  const long long tile_rows = static_cast<long long>(a.rtiles) * a.nkb * 128;
+  if (tiles_total > INT32_MAX || tile_rows > INT32_MAX) return fail(MUSE_ERR_SHAPE, "tc_gemm2: too many tiles");
+  CUtensorMap tmx, tmw;
+  if (int rc = make_map(&tmx, x, m, k, 128)) return rc;
+  // The packed tile array seen as [tiles * 128 rows, 64] BF16: a box is one 16 KB tile, copied as is.
+  if (int rc = make_map(&tmw, tiles, tile_rows, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
+  auto kern = muse::tc_gemm2_kernel;
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaError_t e = cudaSuccess;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_gemm2): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(muse::kG2Threads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(muse::g2_smem(stages));
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 0;  // no programmatic launch with clusters
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cfg.gridDim = dim3(2, 1, 1);
+  int clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+  if (e != cudaSuccess || clusters < 1)
+    return fail(MUSE_ERR_PLAN, "tc_gemm2: CTA pairs cannot be scheduled (%s)", e == cudaSuccess ? "occupancy 0" : cudaGetErrorString(e));
+  long long pairs = p.ctas > 0 ? p.ctas / 2 : clusters;
+  pairs = std::max<long long>(1, std::min<long long>({pairs, static_cast<long long>(clusters), tiles_total}));
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, tmx, tmw, a);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_gemm2 launch: %s", cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -499,6 +623,10 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights_12b, MusePlan
   if (m <= 4 && k % 256 == 0) {
     out->kernel = MUSE_KERNEL_GEMV_BF16;
     out->warps = 8;
+    return MUSE_OK;
+  }
+  if (m > 256) {
+    out->kernel = MUSE_KERNEL_TC_GEMM2;
     return MUSE_OK;
   }
   out->kernel = MUSE_KERNEL_TC_TILE;
@@ -571,8 +699,10 @@ int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, i
     return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles: x and tiles 16-byte aligned, y 2-byte aligned, K % 8 == 0");
   if (plan->kernel == MUSE_KERNEL_TC_STREAMK)
     return run_streamk(x, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
+  if (plan->kernel == MUSE_KERNEL_TC_GEMM) return run_gemm(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
+  if (plan->kernel == MUSE_KERNEL_TC_GEMM2) return run_gemm2(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel != MUSE_KERNEL_TC_TILE)
-    return fail(MUSE_ERR_PLAN, "proj_bf16_tiles: plan kernel must be TC_TILE or TC_STREAMK");
+    return fail(MUSE_ERR_PLAN, "proj_bf16_tiles: plan kernel must be TC_TILE, TC_STREAMK, TC_GEMM or TC_GEMM2");
   return run_tc_tile(x, nullptr, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 

@@ -1,0 +1,206 @@
+// Persistent tcgen05 GEMM over CTA pairs for prefill shapes: y[m, n] = sum_k x[m, k] * W[n, k].
+//
+// A cluster of 2 CTAs computes one 256 (tokens) x 256 (W rows) FP32 tile with cta_group::2 UMMAs
+// (M = 256, N = 256, K = 16): CTA r of the pair holds tokens r * 128 .. + 127 of A and W rows
+// r * 128 .. + 127 of B in its own shared memory, and its TMEM receives its 128 tokens x 256
+// columns of D. Per stage each CTA loads 16 KB of x (2-D TMA, 128-byte swizzle) and one 16 KB
+// packed W tile (2-D TMA over the tile array with no swizzle: the tile is already in swizzled
+// order, so the copy is one contiguous 16 KB read); both loads complete on the even CTA's
+// mbarrier (cta_group::2 form, no multicast), which expects the pair's 64 KB. The even CTA alone
+// issues the UMMAs and commits to both CTAs' barriers. Each CTA only stages half of B, so a
+// stage is 32 KB and six fit: twice the bytes in flight of the single-CTA kernel for the same
+// UMMA work, and half of its B traffic per FLOP.
+//
+// Pairs walk the 256 x 256 tiles persistently, token tile fastest. Two TMEM accumulators
+// (2 x 256 columns) overlap a tile's epilogue with the next tile's UMMAs; the odd CTA's epilogue
+// warps release an accumulator with remote arrives on the even CTA's barrier.
+#pragma once
+
+#include "ptx.cuh"
+#include "tc_gemm.cuh"  // pack_bf16x2
+
+namespace muse {
+
+constexpr int kG2Threads = 192;
+constexpr int kG2Half = 16384;                 // 128 rows x 64 k of BF16
+constexpr int kG2Stage = 2 * kG2Half;          // x half + W half, per CTA
+constexpr uint32_t kG2Cols = 512;
+
+__host__ __device__ constexpr int g2_smem(int stages) { return 1024 + stages * kG2Stage + (2 * stages + 4) * 8 + 16; }
+
+struct G2Args {
+  uint16_t* y;  // [M, N]
+  int M, N, K, stages;
+  int mtiles, ntiles, nkb, rtiles;  // 256-token tiles, 256-row tiles, k blocks, 128-row packed tiles
+  TraceRec* trace;
+  int trace_cap;
+};
+
+__global__ void __launch_bounds__(kG2Threads, 1)
+    tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, const G2Args a) {
+  constexpr uint32_t kIdesc = umma_idesc_bf16(256, 256);
+  extern __shared__ uint8_t smem_raw[];
+  const bool tracing = a.trace != nullptr && static_cast<int>(blockIdx.x) < a.trace_cap && threadIdx.x == 64;
+  const unsigned long long t_start = tracing ? globaltimer() : 0ull;
+  unsigned long long t_ready = 0ull, t_main = 0ull;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stages = a.stages;
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + static_cast<size_t>(stages) * kG2Half;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + static_cast<size_t>(stages) * kG2Half);
+  uint64_t* empty = full + stages;
+  uint64_t* acc_full = empty + stages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2], used in the even CTA: 4 local + 4 remote arrives
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int tiles = a.mtiles * a.ntiles;
+  const int nkb = a.nkb;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmx);
+    prefetch_tensormap(&tmw);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, kG2Cols);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (tracing) t_ready = globaltimer();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_last();  // x and W tiles are re-read by other pairs
+      pdl_wait();
+      long long it = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        const int mt = t % a.mtiles, nt = t / a.mtiles;
+        const int xrow = mt * 256 + static_cast<int>(rank) * 128;
+        int rt = nt * 2 + static_cast<int>(rank);
+        if (rt >= a.rtiles) rt = nt * 2;  // past N: a valid tile; its rows are never stored
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = static_cast<int>(it % stages);
+          if (!mbar_wait(&empty[s], static_cast<uint32_t>((it / stages) & 1) ^ 1u, kErrTcProducer)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_expect_tx(&full[s], static_cast<uint32_t>(2 * kG2Stage));
+          const uint32_t bar = map_peer(smem_u32(&full[s]), 0u);
+          tma_load_2d_pair(sa + static_cast<size_t>(s) * kG2Half, &tmx, bar, kb * 64, xrow, pol);
+          tma_load_2d_pair(sb + static_cast<size_t>(s) * kG2Half, &tmw, bar, 0, (rt * nkb + kb) * 128, pol);
+        }
+      }
+      // Every load this CTA issued is consumed (and so has landed) once its stage is released.
+      const long long issued = it;
+      for (long long i = (issued > stages ? issued - stages : 0); i < issued; ++i)
+        mbar_wait(&empty[i % stages], static_cast<uint32_t>((i / stages) & 1), kErrDrain, kWaitLimitNs / 10);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      long long it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs, ++local) {
+        const int b = local & 1;
+        ok = mbar_wait(&acc_empty[b], static_cast<uint32_t>((local >> 1) & 1) ^ 1u, kErrTcMma);
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(b * 256);
+        for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
+          const int s = static_cast<int>(it % stages);
+          if (!mbar_wait(&full[s], static_cast<uint32_t>((it / stages) & 1), kErrTcMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = umma_desc_sw128(smem_u32(sa + static_cast<size_t>(s) * kG2Half));
+          const uint64_t db = umma_desc_sw128(smem_u32(sb + static_cast<size_t>(s) * kG2Half));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16_pair(d, da + 2 * kk, db + 2 * kk, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_pair_mc(&empty[s], 0x3);
+        }
+        umma_commit_pair_mc(&acc_full[b], 0x3);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const bool vec_ok = (a.N % 8) == 0;
+    bool waited = false;
+    int local = 0;
+    for (int t = pair; t < tiles; t += npairs, ++local) {
+      const int b = local & 1;
+      const int mt = t % a.mtiles, nt = t / a.mtiles;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], static_cast<uint32_t>((local >> 1) & 1),
+                                                        kErrTcEpilogue));
+      tc_fence_after();
+      if (!waited) {
+        if (tracing) t_main = globaltimer();
+        pdl_wait();
+        waited = true;
+      }
+      if (!ok) break;
+      const int m = mt * 256 + static_cast<int>(rank) * 128 + row;
+      const int n0 = nt * 256;
+      uint16_t* yrow = a.y + static_cast<size_t>(m) * a.N;
+#pragma unroll 1
+      for (int c = 0; c < 256; c += 16) {
+        float v[16];
+        tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * 256 + c), v);
+        const int n = n0 + c;
+        if (m < a.M && n < a.N) {
+          if (vec_ok && n + 16 <= a.N) {
+            uint4 p0, p1;
+            p0.x = pack_bf16x2(v[0], v[1]);
+            p0.y = pack_bf16x2(v[2], v[3]);
+            p0.z = pack_bf16x2(v[4], v[5]);
+            p0.w = pack_bf16x2(v[6], v[7]);
+            p1.x = pack_bf16x2(v[8], v[9]);
+            p1.y = pack_bf16x2(v[10], v[11]);
+            p1.z = pack_bf16x2(v[12], v[13]);
+            p1.w = pack_bf16x2(v[14], v[15]);
+            uint4* dst = reinterpret_cast<uint4*>(yrow + n);
+            dst[0] = p0;
+            dst[1] = p1;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (n + j < a.N) yrow[n + j] = f32_to_bf16(v[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_peer(smem_u32(&acc_empty[b]), 0u));
+    }
+    if (!waited) pdl_wait();
+  }
+  pdl_launch_dependents();
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the pair's UMMAs and both epilogues are done before either CTA frees TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kG2Cols);
+  }
+  if (tracing) a.trace[blockIdx.x] = TraceRec{t_start, t_ready, t_main, globaltimer(), smid(), blockIdx.x, 0u, 0u};
+}
+
+}  // namespace muse

@@ -31,7 +31,7 @@ L2_BYTES = 126 * 1024 * 1024
 
 REFERENCE_SHAPES = [(LAYERS[n][0], LAYERS[n][1]) for n in ("qkv_gate", "o", "pooler", "unpooler")] + [(UNPOOL_SLICE, 4096)]
 BASELINE_SHAPES = [BASELINE_LAYERS[n] for n in ("qkv_decode", "qkv_prefill")]
-DEFAULT_MS = [1, 2, 4, 8, 16, 32, 64, 128, 256]
+DEFAULT_MS = [1, 2, 4, 8, 16, 32, 64, 128, 256, 512]
 
 
 def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[str, _lib.MusePlan]]:
@@ -59,6 +59,9 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
                                           flags=_lib.FLAG_GLOBAL_SPLIT)))
         if split <= 4 and tiles * split <= sms:
             out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=bnt, split=split)))
+    if m >= 128:
+        out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM)))
+        out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2)))
     if bnt <= 128:
         for stages, ctas in ((4, 2 * sms), (6, sms), (8, sms)):
             if bnt >= 128 and ctas > sms:

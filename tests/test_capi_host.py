@@ -51,7 +51,9 @@ def test_plan_default_without_device():
     p = _lib.plan_default(16, 6144, 4096)
     assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 16 and 1 <= p.split <= 8
     p = _lib.plan_default(4096, 10240, 8192)
-    assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 256 and p.split == 1
+    assert p.kernel == _lib.KERNEL_TC_GEMM2
+    p = _lib.plan_default(256, 10240, 8192)
+    assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 256
     p = _lib.plan_default(1, 10240, 8192, weights_12b=True)
     assert p.kernel == _lib.KERNEL_GEMV_12B
     with pytest.raises(_lib.MuseError):

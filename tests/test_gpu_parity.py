@@ -349,3 +349,29 @@ def test_tc_streamk_needs_scratch():
     with pytest.raises(_lib.MuseError) as e:
         _lib.proj_bf16_tiles(x.data_ptr(), t.data_ptr(), y.data_ptr(), 4, 256, 1024, plan, stream(), 0, 0)
     assert e.value.code == -4
+
+
+GEMM_CASES = [  # (m, n, k, stages, ctas)
+    (512, 2304, 8192, 4, 0), (1000, 8192, 4096, 4, 0), (300, 1000, 1000, 3, 0), (257, 384, 512, 2, 7),
+    (128, 256, 64, 4, 0), (130, 200, 200, 4, 0), (4096, 1024, 2048, 4, 148), (2048, 640, 4096, 3, 37),
+]
+
+
+@pytest.mark.parametrize("m,n,k,stages,ctas", GEMM_CASES)
+def test_tc_gemm(m, n, k, stages, ctas):
+    xb, wb = _rand_bits((m, k), 90 + m), _rand_bits((n, k), 95 + n, 0.02)
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM, stages=stages, ctas=ctas)
+    y = _run_bf16(xb, wb, plan, tiles=True)
+    assert_parity(xb, wb, y, what=f"gemm m={m} n={n} k={k} stages={stages} ctas={ctas}")
+    y2 = _run_bf16(xb, wb, plan, tiles=True)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+
+
+@pytest.mark.parametrize("m,n,k,stages,ctas", GEMM_CASES + [(256, 512, 128, 6, 2), (600, 300, 4096, 4, 10)])
+def test_tc_gemm_pairs(m, n, k, stages, ctas):
+    xb, wb = _rand_bits((m, k), 190 + m), _rand_bits((n, k), 195 + n, 0.02)
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2, stages=min(stages + 2, 6), ctas=ctas)
+    y = _run_bf16(xb, wb, plan, tiles=True)
+    assert_parity(xb, wb, y, what=f"gemm2 m={m} n={n} k={k} ctas={ctas}")
+    y2 = _run_bf16(xb, wb, plan, tiles=True)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
