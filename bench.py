@@ -225,10 +225,9 @@ def main():
 
     # ---- workload: R rotating copies (each rank: its shard when sharded) ----------------------
     if sharded:
-        if n_full % world:
-            raise SystemExit(f"N={n_full} does not split across {world} ranks")
-        n = n_full // world
-        r0 = rank * n
+        from muse_bf16_proj_b200.sharded import shard_rows
+        r0, r1 = shard_rows(n_full, world, rank)
+        n = r1 - r0
     else:
         n, r0 = n_full, 0
     w_bytes = n * k * (1.5 if fmt == "12b" else 2)
@@ -264,7 +263,8 @@ def main():
 
     gather_out = None
     if sharded and args.gather and world > 1:
-        gather_out = torch.empty((world, m, n), dtype=torch.bfloat16, device=dev)
+        from muse_bf16_proj_b200.sharded import gather_columns
+        gather_out = torch.empty((m, n_full), dtype=torch.bfloat16, device=dev)
 
     # ---- warm-up, clock soak, timed region --------------------------------------------------
     for i in range(max(3, args.warmup)):
@@ -300,7 +300,7 @@ def main():
     for i in range(K):
         step(i)
         if gather_out is not None:
-            dist.all_gather_into_tensor(gather_out, ys[i % rot])
+            gather_columns(ys[i % rot], world, out=gather_out)
     end.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -374,7 +374,8 @@ def main():
         "device_error": code,
     }
     if gather_out is not None:
-        line["config"]["all_gather"] = "NCCL all_gather_into_tensor of y after every step (inside the timed region)"
+        line["config"]["all_gather"] = ("NCCL all_gather_into_tensor of y into [P, M, N/P] plus the copy to [M, N] "
+                                        "after every step, inside the timed region")
     if world == 1 and not args.no_cpu_baseline:
         cpu = CpuReference(m, n, k)
         sec, calls = cpu.timed(args.cpu_seconds, max_calls=30)

@@ -57,6 +57,10 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
             continue
         out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=bnt, split=split,
                                           flags=_lib.FLAG_GLOBAL_SPLIT)))
+        if bnt <= 64:  # rings small enough for two CTAs an SM (the next launch's CTAs co-reside)
+            for stages in (4, 6):
+                out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=bnt, split=split, stages=stages,
+                                                  flags=_lib.FLAG_GLOBAL_SPLIT)))
         if split <= 4 and tiles * split <= sms:
             out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=bnt, split=split)))
     if m >= 128:
