@@ -91,12 +91,17 @@ int muse_sm_count(int* out);
  */
 int muse_device_error(int* code, void* stream);
 
+/* How W is held, for muse_plan_default. */
+#define MUSE_WEIGHTS_ROW_MAJOR 0 /* BF16 [N, K] row-major (muse_proj_bf16) */
+#define MUSE_WEIGHTS_12B 1       /* 12-bit planes (muse_proj_12b) */
+#define MUSE_WEIGHTS_TILES 2     /* packed tiles (muse_proj_bf16_tiles; TC_GEMM2 and TC_STREAMK plans need scratch) */
+
 /*
- * The library's default plan for a shape (weights_12b: 1 when W is 12-bit encoded).
- * Replaces the reference's per-shape tables' fallback rule (submission.py:76-127, 900-908):
- * shapes no table row names get this plan.
+ * The library's default plan for a shape and weight format (MUSE_WEIGHTS_*). Replaces the
+ * reference's per-shape tables' fallback rule (submission.py:76-127, 900-908): shapes no table
+ * row names get this plan.
  */
-int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights_12b, MusePlan* out);
+int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* out);
 
 /*
  * Bytes of device scratch a plan needs (0 for most plans). Scratch holds the per-tile split-K

@@ -129,9 +129,13 @@ def device_error(stream: int = 0) -> int:
     return code.value
 
 
-def plan_default(m: int, n: int, k: int, weights_12b: bool = False) -> MusePlan:
+WEIGHTS_ROW_MAJOR, WEIGHTS_12B, WEIGHTS_TILES = 0, 1, 2
+
+
+def plan_default(m: int, n: int, k: int, weights_12b: bool = False, tiles: bool = False) -> MusePlan:
     p = MusePlan()
-    check(load().muse_plan_default(m, n, k, int(weights_12b), ctypes.byref(p)))
+    fmt = WEIGHTS_12B if weights_12b else (WEIGHTS_TILES if tiles else WEIGHTS_ROW_MAJOR)
+    check(load().muse_plan_default(m, n, k, fmt, ctypes.byref(p)))
     return p
 
 

@@ -606,38 +606,50 @@ int muse_device_error(int* code, void* stream) {
   return MUSE_OK;
 }
 
-int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights_12b, MusePlan* out) {
+int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* out) {
   muse::clear_error();
   if (!out) return fail(MUSE_ERR_INVALID, "plan_default: null output");
   if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "plan_default: non-positive size");
+  if (weights < MUSE_WEIGHTS_ROW_MAJOR || weights > MUSE_WEIGHTS_TILES)
+    return fail(MUSE_ERR_INVALID, "plan_default: weights must be MUSE_WEIGHTS_ROW_MAJOR, _12B or _TILES");
   DeviceInfo* d;
   int sms = 148;
   if (device_info(&d) == MUSE_OK) sms = d->sms;
   muse::clear_error();
   std::memset(out, 0, sizeof(*out));
-  if (weights_12b) {
+  if (weights == MUSE_WEIGHTS_12B) {
     out->kernel = MUSE_KERNEL_GEMV_12B;
-    out->warps = 8;
+    out->warps = 16;
     return m <= 8 ? MUSE_OK : fail(MUSE_ERR_SHAPE, "plan_default: 12-bit weights serve M <= 8");
   }
-  if (m <= 4 && k % 256 == 0) {
-    out->kernel = MUSE_KERNEL_GEMV_BF16;
-    out->warps = 8;
-    return MUSE_OK;
-  }
   if (m > 256) {
+    if (weights != MUSE_WEIGHTS_TILES) return fail(MUSE_ERR_SHAPE, "plan_default: M > 256 needs packed tiles");
     out->kernel = MUSE_KERNEL_TC_GEMM2;
     return MUSE_OK;
   }
-  out->kernel = MUSE_KERNEL_TC_TILE;
   int bnt = 16;
   while (bnt < m && bnt < 256) bnt *= 2;
+  if (weights == MUSE_WEIGHTS_TILES && m <= 128) {
+    // Stream-K: every SM streams the same share of W in one wave.
+    out->kernel = MUSE_KERNEL_TC_STREAMK;
+    out->tile_n = bnt;
+    out->stages = 4;
+    out->ctas = bnt <= 64 ? 2 * sms : sms;
+    return MUSE_OK;
+  }
+  if (weights == MUSE_WEIGHTS_ROW_MAJOR && m <= 4 && k % 256 == 0) {
+    out->kernel = MUSE_KERNEL_GEMV_BF16;
+    out->warps = 16;
+    return MUSE_OK;
+  }
+  out->kernel = MUSE_KERNEL_TC_TILE;
   out->tile_n = bnt;
   const int64_t tiles = ((n + 127) / 128) * ((m + bnt - 1) / bnt);
   const int64_t nkb = (k + 63) / 64;
   int64_t split = tiles >= sms ? 1 : sms / tiles;
   split = std::max<int64_t>(1, std::min<int64_t>({split, 8, nkb}));
   out->split = static_cast<int>(split);
+  if (split > 1 && weights == MUSE_WEIGHTS_TILES) out->flags = MUSE_FLAG_GLOBAL_SPLIT;
   return MUSE_OK;
 }
 

@@ -37,16 +37,17 @@ class Dispatch:
                 return e
         return None
 
-    def plan(self, m: int, n: int, k: int, have_12b: bool = False) -> tuple[_lib.MusePlan, str]:
-        """(plan, weight format) for y[m, n] = x[m, k] W[n, k]^T."""
-        key = (m, n, k, have_12b)
+    def plan(self, m: int, n: int, k: int, have_12b: bool = False, tiles: bool = True) -> tuple[_lib.MusePlan, str]:
+        """(plan, weight format) for y[m, n] = x[m, k] W[n, k]^T; `tiles`: a packed copy of W
+        exists (table rows assume it, as prepare makes one)."""
+        key = (m, n, k, have_12b, tiles)
         hit = self._cache.get(key)
         if hit is None:
             e = self._match(m, n, k, have_12b)
             if e is not None:
                 hit = (_lib.MusePlan.from_dict(e["plan"]), e.get("weights", "bf16"))
             else:
-                hit = (_lib.plan_default(m, n, k, False), "bf16")
+                hit = (_lib.plan_default(m, n, k, False, tiles=tiles), "bf16")
             self._cache[key] = hit
         return hit
 

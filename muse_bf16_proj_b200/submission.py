@@ -161,7 +161,7 @@ def _known_answer_check(state: dict, layer: str, n: int, m: int) -> None:
     x = x.to(torch.bfloat16)
     y = project(x, state, layer, n).float()
     expect = (w[:n].float()[:, cols].T * powers[:, None]).to(torch.bfloat16).float()
-    plan, fmt = state["dispatch"].plan(m, n, k, layer in state["enc12"])
+    plan, fmt = state["dispatch"].plan(m, n, k, layer in state["enc12"], tiles=layer in state["tiles"])
     if fmt == "12b":
         err = ((y - expect).norm(dim=1) / expect.norm(dim=1).clamp(min=1e-30)).max().item()
         ok = err <= 1e-3
@@ -192,7 +192,7 @@ def project(x: torch.Tensor, state: dict, layer: str, n: int | None = None,
         x = x.clone()  # the kernels read x with 16-byte vector loads / TMA
     m = x.shape[0]
     enc = state["enc12"].get(layer)
-    plan, fmt = state["dispatch"].plan(m, n, k, enc is not None)
+    plan, fmt = state["dispatch"].plan(m, n, k, enc is not None, tiles=layer in state["tiles"])
     if state.get("pdl", True) and not plan.flags & _lib.FLAG_PDL:
         # The weights are prepare-time constants, so the kernel may stream them before the
         # previous kernel in the stream has finished (programmatic dependent launch).

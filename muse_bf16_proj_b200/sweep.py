@@ -31,6 +31,8 @@ L2_BYTES = 126 * 1024 * 1024
 
 REFERENCE_SHAPES = [(LAYERS[n][0], LAYERS[n][1]) for n in ("qkv_gate", "o", "pooler", "unpooler")] + [(UNPOOL_SLICE, 4096)]
 BASELINE_SHAPES = [BASELINE_LAYERS[n] for n in ("qkv_decode", "qkv_prefill")]
+# The column-parallel MLP-up weight's per-GPU shards at 1, 2, 4 and 8 GPUs.
+MLP_SHARD_SHAPES = [(BASELINE_LAYERS["mlp_up"][0] // p, BASELINE_LAYERS["mlp_up"][1]) for p in (1, 2, 4, 8)]
 DEFAULT_MS = [1, 2, 4, 8, 16, 32, 64, 128, 256, 512]
 
 
@@ -292,6 +294,8 @@ def main():
             shapes += REFERENCE_SHAPES
         elif s == "baseline":
             shapes += BASELINE_SHAPES
+        elif s == "mlp":
+            shapes += MLP_SHARD_SHAPES
         elif "x" in s:
             a, b = s.split("x")
             shapes.append((int(a), int(b)))

@@ -48,12 +48,16 @@ def test_proj_argument_errors_before_any_device_work():
 def test_plan_default_without_device():
     p = _lib.plan_default(1, 6144, 4096)
     assert p.kernel == _lib.KERNEL_GEMV_BF16
+    p = _lib.plan_default(1, 6144, 4096, tiles=True)
+    assert p.kernel == _lib.KERNEL_TC_STREAMK and p.tile_n == 16
     p = _lib.plan_default(16, 6144, 4096)
     assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 16 and 1 <= p.split <= 8
-    p = _lib.plan_default(4096, 10240, 8192)
-    assert p.kernel == _lib.KERNEL_TC_GEMM2
-    p = _lib.plan_default(256, 10240, 8192)
+    p = _lib.plan_default(200, 6144, 4096, tiles=True)
     assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 256
+    p = _lib.plan_default(4096, 10240, 8192, tiles=True)
+    assert p.kernel == _lib.KERNEL_TC_GEMM2
+    with pytest.raises(_lib.MuseError):
+        _lib.plan_default(4096, 10240, 8192)  # needs packed tiles
     p = _lib.plan_default(1, 10240, 8192, weights_12b=True)
     assert p.kernel == _lib.KERNEL_GEMV_12B
     with pytest.raises(_lib.MuseError):
@@ -73,7 +77,9 @@ def test_dispatch_table_lookup_and_defaults():
     assert fmt == "bf16" and plan.kernel == _lib.KERNEL_GEMV_BF16 and plan.warps == 16
     plan, fmt = d.plan(17, 6144, 4096)
     assert plan.kernel == _lib.KERNEL_TC_TILE and plan.split == 3 and plan.tile_n == 32
-    plan, fmt = d.plan(64, 6144, 4096)   # no row: library default
+    plan, fmt = d.plan(64, 6144, 4096)   # no row: library default (packed tiles)
+    assert plan.kernel == _lib.KERNEL_TC_STREAMK and plan.tile_n == 64
+    plan, fmt = d.plan(64, 6144, 4096, tiles=False)
     assert plan.kernel == _lib.KERNEL_TC_TILE and plan.tile_n == 64
     assert d.wants_12b(6144, 4096) and not d.wants_12b(6144, 8192)
     assert _lib.MusePlan.from_dict(plan.as_dict()).key() == plan.key()

@@ -1,0 +1,61 @@
+"""The N-sharded projection on 2 GPUs with NCCL: each rank runs the sm_100a kernels on its W shard,
+the all-gather rebuilds y, checked against the FP64 oracle. Skipped with fewer than 2 GPUs."""
+
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from muse_bf16_proj_b200.sharded import ShardedProjection
+        from oracle import contract_ref as O
+
+        out = {}
+        for m, n, k in ((1, 2048, 4096), (16, 4096, 4096), (512, 2048, 2048)):
+            g = torch.Generator().manual_seed(m + n)
+            w = (torch.randn((n, k), generator=g) * 0.02).to(torch.bfloat16)
+            x = torch.randn((m, k), generator=g).to(torch.bfloat16)
+            sp = ShardedProjection(w.cuda(), n, verbose=False)
+            y = sp.gather(sp.project(x.cuda()))
+            torch.cuda.synchronize()
+            yb = y.cpu().view(torch.int16).numpy().view(np.uint16)
+            xb = x.view(torch.int16).numpy().view(np.uint16)
+            wb = w.view(torch.int16).numpy().view(np.uint16)
+            ok, msg, _ = O.check_implementation(xb, wb, yb)
+            out[(m, n, k)] = (ok, msg)
+        results[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_projection_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    mp.start_processes(_worker, args=(2, _free_port(), results), nprocs=2, join=True, start_method="spawn")
+    for rank in range(2):
+        for shape, (ok, msg) in results[rank].items():
+            assert ok, f"rank {rank} {shape}: {msg}"
