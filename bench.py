@@ -242,8 +242,9 @@ def main():
         del w
     torch.cuda.empty_cache()
     entries = None
-    if fmt == "12b":
-        entries = [{"n": n, "k": k, "m_lo": 1, "m_hi": 8, "weights": "12b", "plan": {"kernel": "gemv_12b"}}]
+    if fmt == "12b" and not Dispatch().wants_12b(n, k):  # no table row: the library's 12-bit tile plan
+        entries = [{"n": n, "k": k, "m_lo": m, "m_hi": m, "weights": "12b",
+                    "plan": _lib.plan_default(m, n, k, weights_12b=True, tiles=True).as_dict()}]
     if args.plan:
         entries = [{"n": n, "k": k, "m_lo": m, "m_hi": m, "weights": fmt, "plan": json.loads(args.plan)}]
     disp = Dispatch(entries=entries) if entries is not None else Dispatch()

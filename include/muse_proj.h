@@ -37,6 +37,8 @@ extern "C" {
 #define MUSE_KERNEL_TC_STREAMK 4 /* tcgen05 stream-K over packed tiles: equal work per CTA, one wave */
 #define MUSE_KERNEL_TC_GEMM 5    /* persistent tcgen05 GEMM, 128 tokens x 256 W rows a tile (prefill) */
 #define MUSE_KERNEL_TC_GEMM2 6   /* persistent tcgen05 GEMM on CTA pairs (cta_group::2), 256 x 256 a tile */
+#define MUSE_KERNEL_TC_12B 7     /* stream-K tcgen05 on 12-bit tiles: W decoded to BF16 in shared memory */
+#define MUSE_KERNEL_TC_SKINNY 8  /* stream-K tcgen05 over packed tiles with W as the B operand (256 W rows an MMA) */
 
 /* Plan flags. */
 #define MUSE_FLAG_GLOBAL_SPLIT 1 /* TC_TILE: reduce K-split partials through caller scratch instead of a cluster */
@@ -49,11 +51,11 @@ extern "C" {
 typedef struct MusePlan {
   int32_t kernel; /* MUSE_KERNEL_* */
   int32_t split;  /* TC_TILE: CTAs splitting K (cluster: 1..16; global: 1..64) */
-  int32_t tile_n; /* TC_TILE: tokens per tile, 16/32/64/128/256 */
+  int32_t tile_n; /* tensor-core kernels: tokens per tile, 16/32/64/128 (TC_TILE, TC_STREAMK also 256) */
   int32_t stages; /* shared-memory ring depth (0 = kernel default) */
-  int32_t ctas;   /* GEMV, TC_STREAMK: CTAs in the grid (0 = one per SM) */
+  int32_t ctas;   /* GEMV, TC_STREAMK, TC_SKINNY, TC_12B: CTAs in the grid (0 = one per SM) */
   int32_t warps;  /* GEMV: consumer warps per CTA: 4, 8 or 16 (0 = 8) */
-  int32_t chunk;  /* GEMV: units per bulk copy (0 = about 16 KB) */
+  int32_t chunk;  /* GEMV: units per bulk copy (0 = about 16 KB); TC_12B: decoded-tile ring depth 1..4 (0 = 2) */
   int32_t flags;  /* MUSE_FLAG_* */
 } MusePlan;
 
@@ -95,6 +97,7 @@ int muse_device_error(int* code, void* stream);
 #define MUSE_WEIGHTS_ROW_MAJOR 0 /* BF16 [N, K] row-major (muse_proj_bf16) */
 #define MUSE_WEIGHTS_12B 1       /* 12-bit planes (muse_proj_12b) */
 #define MUSE_WEIGHTS_TILES 2     /* packed tiles (muse_proj_bf16_tiles; TC_GEMM2 and TC_STREAMK plans need scratch) */
+#define MUSE_WEIGHTS_12B_TILES 3 /* 12-bit tiles (muse_proj_12b_tiles; needs scratch) */
 
 /*
  * The library's default plan for a shape and weight format (MUSE_WEIGHTS_*). Replaces the
@@ -141,7 +144,8 @@ int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stre
 /*
  * y = x . W^T with W given as packed tiles (muse_pack_tiles of the full W: the first
  * ceil(n / 128) row tiles serve W[:n]). plan->kernel: MUSE_KERNEL_TC_TILE,
- * MUSE_KERNEL_TC_STREAMK (which always needs scratch, see muse_scratch_bytes) or
+ * MUSE_KERNEL_TC_STREAMK or MUSE_KERNEL_TC_SKINNY (both always need scratch, see
+ * muse_scratch_bytes; TC_SKINNY reads two tiles a k block as one 256-row B operand) or
  * MUSE_KERNEL_TC_GEMM / MUSE_KERNEL_TC_GEMM2 (prefill; replace the cuBLAS F.linear that served
  * the reference's large shapes, submission.py:1170). Each pipeline
  * stage moves one contiguous 16 KB tile with a 1-D bulk copy. Replaces TmaGemm.__call__
@@ -177,6 +181,35 @@ int muse_proj_bf16_tiles_noalloc(const void* x, const void* tiles, void* y, int6
  * (submission.py:660-673, 357-474). plan->kernel must be MUSE_KERNEL_GEMV_12B; M <= 8.
  */
 int muse_proj_12b(const MuseEnc12* enc, const void* x, void* y, int64_t m, const MusePlan* plan, void* stream);
+
+/* Device bytes of the 12-bit tile copy muse_pack_tiles12 writes: ceil(N / 128) * (K / 64) * 12416. */
+int muse_tiles12_bytes(int64_t n, int64_t k, int64_t* bytes);
+
+/*
+ * Re-lays enc's 12-bit weights (device) into blocks of 128 rows x 64 k, 12416 bytes each,
+ * ordered [row tile][k block]; rows past N are zero (two device kernels on `stream`):
+ *   bytes 0 .. 12287: six 2048-byte slabs of 128 16-byte chunks (row r at r * 16). Slab j < 4
+ *     holds the low bytes of weights 16j .. 16j + 15; slab 4 + j the code bytes of weights
+ *     32j .. 32j + 31 (byte i = codes of weights 2i and 2i + 1, low nibble first);
+ *   bytes 12288 .. 12415: u32 word 0 = the tile's window base << 16 | the block's escape count;
+ *     words 1 .. 31 = its first 31 escapes as r << 22 | (k - 64 * block) << 16 | BF16 bits,
+ *     sorted by row then k (a block with more is served from enc's per-row list).
+ * No counterpart in the reference (its nf12 planes are read row-major by CUDA cores,
+ * submission.py:268-271).
+ */
+int muse_pack_tiles12(const MuseEnc12* enc, void* tiles12, void* stream);
+
+/*
+ * y = x . decode12(W)^T on the tensor cores from the 12-bit tiles (muse_pack_tiles12) and enc's
+ * per-row escape list (enc->planes and enc->bases are not read). Every BF16 weight reaching the
+ * UMMA equals the original bit for bit, so the result matches a BF16 GEMM on the original W with
+ * the same K split. Replaces nf12_cuda_gemv / nf12_gemv (submission.py:660-673, 357-474), which
+ * serve M <= 16 on CUDA cores; any M here. plan->kernel must be MUSE_KERNEL_TC_12B. Needs
+ * muse_scratch_bytes of scratch, 256-byte aligned, zeroed before its first use (every launch
+ * leaves it zeroed again).
+ */
+int muse_proj_12b_tiles(const MuseEnc12* enc, const void* tiles12, const void* x, void* y, int64_t m,
+                        const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream);
 
 /* Host buffer sizes for muse_encode12: planes and bases bytes. */
 int muse_encode12_sizes(int64_t n, int64_t k, int64_t* planes_bytes, int64_t* bases_bytes);

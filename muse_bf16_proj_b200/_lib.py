@@ -17,9 +17,11 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 MUSE_OK = 0
 ERRORS = {-1: "INVALID", -2: "ALIGN", -3: "SHAPE", -4: "CAPACITY", -5: "CUDA", -6: "TIMEOUT", -7: "PLAN"}
 KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_GEMM, KERNEL_TC_GEMM2 = 1, 2, 3, 4, 5, 6
+KERNEL_TC_12B, KERNEL_TC_SKINNY = 7, 8
 KERNEL_NAMES = {KERNEL_GEMV_BF16: "gemv_bf16", KERNEL_GEMV_12B: "gemv_12b", KERNEL_TC_TILE: "tc_tile",
-                KERNEL_TC_STREAMK: "tc_streamk", KERNEL_TC_GEMM: "tc_gemm", KERNEL_TC_GEMM2: "tc_gemm2"}
-TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_GEMM, KERNEL_TC_GEMM2)
+                KERNEL_TC_STREAMK: "tc_streamk", KERNEL_TC_GEMM: "tc_gemm", KERNEL_TC_GEMM2: "tc_gemm2",
+                KERNEL_TC_12B: "tc_12b", KERNEL_TC_SKINNY: "tc_skinny"}
+TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_SKINNY, KERNEL_TC_GEMM, KERNEL_TC_GEMM2)
 KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
 FLAG_GLOBAL_SPLIT = 1
 FLAG_PDL = 2
@@ -75,6 +77,9 @@ _SIGNATURES = {
     "muse_pack_tiles": ([_P, _P, _I64, _I64, _P], _I32),
     "muse_proj_bf16_tiles": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
     "muse_proj_12b": ([ctypes.POINTER(MuseEnc12), _P, _P, _I64, ctypes.POINTER(MusePlan), _P], _I32),
+    "muse_tiles12_bytes": ([_I64, _I64, ctypes.POINTER(_I64)], _I32),
+    "muse_pack_tiles12": ([ctypes.POINTER(MuseEnc12), _P, _P], _I32),
+    "muse_proj_12b_tiles": ([ctypes.POINTER(MuseEnc12), _P, _P, _P, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
     "muse_proj_bf16_tiles_noalloc": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P], _I32),
     "muse_encode12_sizes": ([_I64, _I64, ctypes.POINTER(_I64), ctypes.POINTER(_I64)], _I32),
     "muse_encode12": ([_P, _I64, _I64, _P, _P, _P, _P, _I64, ctypes.POINTER(_I64), _I32], _I32),
@@ -129,12 +134,16 @@ def device_error(stream: int = 0) -> int:
     return code.value
 
 
-WEIGHTS_ROW_MAJOR, WEIGHTS_12B, WEIGHTS_TILES = 0, 1, 2
+WEIGHTS_ROW_MAJOR, WEIGHTS_12B, WEIGHTS_TILES, WEIGHTS_12B_TILES = 0, 1, 2, 3
 
 
 def plan_default(m: int, n: int, k: int, weights_12b: bool = False, tiles: bool = False) -> MusePlan:
+    """The library's default plan; weights_12b with tiles means the 12-bit tiles (TC_12B)."""
     p = MusePlan()
-    fmt = WEIGHTS_12B if weights_12b else (WEIGHTS_TILES if tiles else WEIGHTS_ROW_MAJOR)
+    if weights_12b:
+        fmt = WEIGHTS_12B_TILES if tiles else WEIGHTS_12B
+    else:
+        fmt = WEIGHTS_TILES if tiles else WEIGHTS_ROW_MAJOR
     check(load().muse_plan_default(m, n, k, fmt, ctypes.byref(p)))
     return p
 
@@ -169,6 +178,22 @@ def pack_tiles(w_ptr: int, tiles_ptr: int, n: int, k: int, stream: int) -> None:
 
 def proj_12b(enc: MuseEnc12, x_ptr: int, y_ptr: int, m: int, plan: MusePlan, stream: int) -> None:
     check(load().muse_proj_12b(ctypes.byref(enc), x_ptr, y_ptr, m, ctypes.byref(plan), ctypes.c_void_p(stream)))
+
+
+def tiles12_bytes(n: int, k: int) -> int:
+    out = ctypes.c_int64()
+    check(load().muse_tiles12_bytes(n, k, ctypes.byref(out)))
+    return out.value
+
+
+def pack_tiles12(enc: MuseEnc12, tiles12_ptr: int, stream: int) -> None:
+    check(load().muse_pack_tiles12(ctypes.byref(enc), tiles12_ptr, ctypes.c_void_p(stream)))
+
+
+def proj_12b_tiles(enc: MuseEnc12, tiles12_ptr: int, x_ptr: int, y_ptr: int, m: int, plan: MusePlan, stream: int,
+                   scratch_ptr: int = 0, scratch_bytes: int = 0) -> None:
+    check(load().muse_proj_12b_tiles(ctypes.byref(enc), tiles12_ptr, x_ptr, y_ptr, m, ctypes.byref(plan),
+                                     scratch_ptr or None, scratch_bytes, ctypes.c_void_p(stream)))
 
 
 TRACE_RECORD_BYTES = 48

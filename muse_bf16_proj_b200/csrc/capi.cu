@@ -1,5 +1,5 @@
 // C ABI of libmuse_proj.so: argument checks, plans, TMA descriptors and kernel launches.
-// The kernels live in gemv.cuh and tc_tile.cuh; this is the only translation unit with device
+// The kernels live in the .cuh headers included below; this is the only translation unit with device
 // code, so the device error word in ptx.cuh has one definition.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -18,6 +18,8 @@
 #include "tc_streamk.cuh"
 #include "tc_gemm.cuh"
 #include "tc_gemm2.cuh"
+#include "tc12.cuh"
+#include "tc_skinny.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -575,6 +577,149 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   return MUSE_OK;
 }
 
+// ---- stream-K skinny kernel: W as the UMMA's B operand (BF16 tiles or 12-bit blocks) -----------
+
+struct SnShape {
+  int bnt, stages, dstages, g, smax;
+  int rtiles, rpairs, nkb, ttiles;
+  long long units, tiles;
+  int64_t scratch;
+};
+
+int sn_shape(bool twelve, int64_t m, int64_t n, int64_t k, const MusePlan& p, SnShape* out) {
+  DeviceInfo* d;
+  int sms = 148, limit = kSmemLimit;
+  if (device_info(&d) == MUSE_OK) {
+    sms = d->sms;
+    limit = std::min(kSmemLimit, d->smem_optin);
+  }
+  muse::clear_error();
+  const char* name = twelve ? "tc_12b" : "tc_skinny";
+  if (twelve && (k < 512 || k % 512 || k > 65536))
+    return fail(MUSE_ERR_SHAPE, "%s: K must be a multiple of 512 and <= 65536", name);
+  if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "%s: dimension too large", name);
+  int bnt = p.tile_n;
+  if (bnt == 0) {
+    bnt = 16;
+    while (bnt < m && bnt < 128) bnt *= 2;
+  }
+  if (bnt != 16 && bnt != 32 && bnt != 64 && bnt != 128)
+    return fail(MUSE_ERR_PLAN, "%s: tile_n must be 16, 32, 64 or 128 (got %d)", name, bnt);
+  const int dstages = twelve ? (p.chunk > 0 ? p.chunk : 2) : 0;
+  if (dstages > 4) return fail(MUSE_ERR_PLAN, "%s: chunk (decoded-tile stages) must be 1..4 (got %d)", name, dstages);
+  const int per_stage = muse::sn_xbytes(bnt) + muse::sn_wbytes(twelve) + 32;
+  const int max_stages = (limit - muse::sn_smem(twelve, bnt, 0, dstages)) / per_stage;
+  const int stages = p.stages > 0 ? p.stages : std::min(twelve ? 6 : 5, max_stages);
+  if (stages < 2 || stages > max_stages)
+    return fail(MUSE_ERR_PLAN, "%s: %d stages do not fit (max %d)", name, stages, max_stages);
+  SnShape sh;
+  sh.bnt = bnt;
+  sh.stages = stages;
+  sh.dstages = dstages;
+  sh.rtiles = static_cast<int>((n + 127) / 128);
+  sh.rpairs = (sh.rtiles + 1) / 2;
+  sh.nkb = static_cast<int>((k + 63) / 64);
+  sh.ttiles = static_cast<int>((m + bnt - 1) / bnt);
+  sh.tiles = static_cast<long long>(sh.rpairs) * sh.ttiles;
+  sh.units = sh.tiles * sh.nkb;
+  if (sh.tiles > kMaxCounters)
+    return fail(MUSE_ERR_SHAPE, "%s: %lld output tiles exceed the %lld counters", name, sh.tiles, (long long)kMaxCounters);
+  long long g = p.ctas > 0 ? p.ctas : sms;
+  sh.g = static_cast<int>(std::min<long long>(g, sh.units));
+  int smax = 1;
+  for (long long t = 0; t < sh.tiles; ++t) {
+    const int a0 = muse::t12_owner(t * sh.nkb, sh.units, sh.g);
+    const int a1 = muse::t12_owner((t + 1) * sh.nkb - 1, sh.units, sh.g);
+    smax = std::max(smax, a1 - a0 + 1);
+  }
+  sh.smax = smax;
+  sh.scratch = kCounterBytes + static_cast<int64_t>(sh.tiles) * smax * bnt * muse::kSnRows * 4;
+  *out = sh;
+  return MUSE_OK;
+}
+
+template <bool kTwelve, int BNT>
+int launch_sn_t(const CUtensorMap& tmx, const muse::SnArgs& a, int g, bool pdl, cudaStream_t st) {
+  auto kern = muse::tc_skinny_kernel<kTwelve, BNT>;
+  // Every CTA holds all 512 TMEM columns: ask for more than half an SM's shared memory so that
+  // no two CTAs (of this or the next launch) share an SM.
+  const int smem = std::max(muse::sn_smem(kTwelve, BNT, a.stages, a.dstages), 116 * 1024);
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaError_t e = cudaSuccess;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_skinny): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(g), 1, 1);
+  cfg.blockDim = dim3(muse::sn_threads(kTwelve), 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, tmx, a);
+  if (e != cudaSuccess)
+    return fail(MUSE_ERR_CUDA, "%s launch (%d CTAs, tile %d): %s", kTwelve ? "tc_12b" : "tc_skinny", g, BNT,
+                cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
+// W: packed BF16 tiles (twelve = false) or 12-bit blocks with enc's escape list (twelve = true).
+int run_skinny(bool twelve, const void* w, const MuseEnc12* enc, const void* x, void* y, int64_t m, int64_t n,
+               int64_t k, const MusePlan& p, void* scratch, int64_t scratch_bytes, cudaStream_t st) {
+  SnShape sh;
+  if (int rc = sn_shape(twelve, m, n, k, p, &sh)) return rc;
+  const char* name = twelve ? "tc_12b" : "tc_skinny";
+  if (!scratch || scratch_bytes < sh.scratch)
+    return fail(MUSE_ERR_CAPACITY, "%s: needs %lld bytes of zeroed scratch (got %lld)", name, (long long)sh.scratch,
+                (long long)(scratch ? scratch_bytes : 0));
+  if (reinterpret_cast<uintptr_t>(scratch) & 255u) return fail(MUSE_ERR_ALIGN, "%s: scratch must be 256-byte aligned", name);
+  CUtensorMap tmx;
+  if (int rc = make_map(&tmx, x, m, k, sh.bnt)) return rc;
+  muse::SnArgs a;
+  a.w = static_cast<const uint8_t*>(w);
+  a.esc_ptr = twelve ? enc->esc_ptr : nullptr;
+  a.esc_val = twelve ? enc->esc_val : nullptr;
+  a.y = static_cast<uint16_t*>(y);
+  a.counters = static_cast<int*>(scratch);
+  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kCounterBytes);
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.stages = sh.stages;
+  a.dstages = sh.dstages;
+  a.rtiles = sh.rtiles;
+  a.rpairs = sh.rpairs;
+  a.nkb = sh.nkb;
+  a.ttiles = sh.ttiles;
+  a.units = sh.units;
+  a.smax = sh.smax;
+  a.y_vec = (n % 8 == 0 && aligned16(y)) ? 1 : 0;
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  const bool pdl = (p.flags & MUSE_FLAG_PDL) != 0;
+  if (twelve) {
+    switch (sh.bnt) {
+      case 16: return launch_sn_t<true, 16>(tmx, a, sh.g, pdl, st);
+      case 32: return launch_sn_t<true, 32>(tmx, a, sh.g, pdl, st);
+      case 64: return launch_sn_t<true, 64>(tmx, a, sh.g, pdl, st);
+      default: return launch_sn_t<true, 128>(tmx, a, sh.g, pdl, st);
+    }
+  }
+  switch (sh.bnt) {
+    case 16: return launch_sn_t<false, 16>(tmx, a, sh.g, pdl, st);
+    case 32: return launch_sn_t<false, 32>(tmx, a, sh.g, pdl, st);
+    case 64: return launch_sn_t<false, 64>(tmx, a, sh.g, pdl, st);
+    default: return launch_sn_t<false, 128>(tmx, a, sh.g, pdl, st);
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -610,8 +755,8 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
   muse::clear_error();
   if (!out) return fail(MUSE_ERR_INVALID, "plan_default: null output");
   if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "plan_default: non-positive size");
-  if (weights < MUSE_WEIGHTS_ROW_MAJOR || weights > MUSE_WEIGHTS_TILES)
-    return fail(MUSE_ERR_INVALID, "plan_default: weights must be MUSE_WEIGHTS_ROW_MAJOR, _12B or _TILES");
+  if (weights < MUSE_WEIGHTS_ROW_MAJOR || weights > MUSE_WEIGHTS_12B_TILES)
+    return fail(MUSE_ERR_INVALID, "plan_default: weights must be MUSE_WEIGHTS_ROW_MAJOR, _12B, _TILES or _12B_TILES");
   DeviceInfo* d;
   int sms = 148;
   if (device_info(&d) == MUSE_OK) sms = d->sms;
@@ -621,6 +766,17 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
     out->kernel = MUSE_KERNEL_GEMV_12B;
     out->warps = 16;
     return m <= 8 ? MUSE_OK : fail(MUSE_ERR_SHAPE, "plan_default: 12-bit weights serve M <= 8");
+  }
+  if (weights == MUSE_WEIGHTS_12B_TILES) {
+    // Stream-K over the 12-bit blocks: one CTA an SM with a deep ring.
+    if (k % 512 || k > 65536) return fail(MUSE_ERR_SHAPE, "plan_default: 12-bit tiles need K % 512 == 0, K <= 65536");
+    int bnt = 16;
+    while (bnt < m && bnt < 128) bnt *= 2;
+    out->kernel = MUSE_KERNEL_TC_12B;
+    out->tile_n = bnt;
+    out->chunk = 2;
+    out->ctas = sms;
+    return MUSE_OK;
   }
   if (m > 256) {
     if (weights != MUSE_WEIGHTS_TILES) return fail(MUSE_ERR_SHAPE, "plan_default: M > 256 needs packed tiles");
@@ -695,6 +851,12 @@ int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, in
     *bytes = sk.scratch;
     return MUSE_OK;
   }
+  if (plan->kernel == MUSE_KERNEL_TC_12B || plan->kernel == MUSE_KERNEL_TC_SKINNY) {
+    SnShape sn;
+    if (int rc = sn_shape(plan->kernel == MUSE_KERNEL_TC_12B, m, n, k, *plan, &sn)) return rc;
+    *bytes = sn.scratch;
+    return MUSE_OK;
+  }
   if (plan->kernel != MUSE_KERNEL_TC_TILE) return MUSE_OK;
   TcShape sh;
   if (int rc = tc_shape(m, n, k, *plan, &sh)) return rc;
@@ -711,10 +873,12 @@ int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, i
     return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles: x and tiles 16-byte aligned, y 2-byte aligned, K % 8 == 0");
   if (plan->kernel == MUSE_KERNEL_TC_STREAMK)
     return run_streamk(x, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
+  if (plan->kernel == MUSE_KERNEL_TC_SKINNY)
+    return run_skinny(false, tiles, nullptr, x, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_GEMM) return run_gemm(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_GEMM2) return run_gemm2(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel != MUSE_KERNEL_TC_TILE)
-    return fail(MUSE_ERR_PLAN, "proj_bf16_tiles: plan kernel must be TC_TILE, TC_STREAMK, TC_GEMM or TC_GEMM2");
+    return fail(MUSE_ERR_PLAN, "proj_bf16_tiles: plan kernel must be TC_TILE, TC_STREAMK, TC_SKINNY, TC_GEMM or TC_GEMM2");
   return run_tc_tile(x, nullptr, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 
@@ -762,6 +926,51 @@ int muse_proj_12b(const MuseEnc12* enc, const void* x, void* y, int64_t m, const
   if (int rc = plan_gemv(true, m, enc->n, enc->k, *plan, a, &grid, &smem, &warps)) return rc;
   return launch_gemv<true>(a, static_cast<int>(m), warps, grid, smem, (plan->flags & MUSE_FLAG_PDL) != 0,
                            static_cast<cudaStream_t>(stream));
+}
+
+int muse_tiles12_bytes(int64_t n, int64_t k, int64_t* bytes) {
+  muse::clear_error();
+  if (!bytes) return fail(MUSE_ERR_INVALID, "tiles12_bytes: null output");
+  if (n < 1 || k < 512) return fail(MUSE_ERR_INVALID, "tiles12_bytes: need N >= 1 and K >= 512");
+  if (k % 512 || k > 65536) return fail(MUSE_ERR_SHAPE, "tiles12_bytes: need K % 512 == 0 and K <= 65536");
+  *bytes = ((n + 127) / 128) * (k / 64) * int64_t(muse::kT12Block);
+  return MUSE_OK;
+}
+
+int muse_pack_tiles12(const MuseEnc12* enc, void* tiles12, void* stream) {
+  muse::clear_error();
+  if (!enc || !enc->planes || !enc->bases || !enc->esc_ptr || (enc->n_esc > 0 && !enc->esc_val) || !tiles12)
+    return fail(MUSE_ERR_INVALID, "pack_tiles12: null pointer");
+  if (enc->n < 1 || enc->k < 512) return fail(MUSE_ERR_INVALID, "pack_tiles12: need N >= 1 and K >= 512");
+  if (enc->k % 512 || enc->k > 65536 || enc->n > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "pack_tiles12: need K % 512 == 0, K <= 65536 and N <= 2^24");
+  if (!aligned16(enc->planes) || !aligned16(tiles12)) return fail(MUSE_ERR_ALIGN, "pack_tiles12: 16-byte alignment needed");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nkb = static_cast<int>(enc->k / 64);
+  const long long blocks12 = ((enc->n + 127) / 128) * static_cast<long long>(nkb);
+  const long long chunks = blocks12 * (muse::kT12Raw / 16);
+  const int grid = static_cast<int>(std::min<long long>((chunks + 255) / 256, 148 * 32));
+  muse::pack_tiles12_kernel<<<grid, 256, 0, st>>>(enc->planes, static_cast<uint8_t*>(tiles12), static_cast<int>(enc->n),
+                                                  static_cast<int>(enc->k), nkb, chunks);
+  if (int rc = launch_error("pack_tiles12 launch")) return rc;
+  if (blocks12 > 0x7FFFFFFFll) return fail(MUSE_ERR_SHAPE, "pack_tiles12: too many blocks");
+  muse::pack_escapes12_kernel<<<static_cast<unsigned>(blocks12), 128, 0, st>>>(
+      enc->bases, enc->esc_ptr, enc->esc_val, static_cast<uint8_t*>(tiles12), static_cast<int>(enc->n),
+      static_cast<int>(enc->k), nkb);
+  return launch_error("pack_escapes12 launch");
+}
+
+int muse_proj_12b_tiles(const MuseEnc12* enc, const void* tiles12, const void* x, void* y, int64_t m,
+                        const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream) {
+  muse::clear_error();
+  if (!enc || !tiles12 || !x || !y || !plan || !enc->esc_ptr || (enc->n_esc > 0 && !enc->esc_val))
+    return fail(MUSE_ERR_INVALID, "proj_12b_tiles: null pointer");
+  if (m < 1 || enc->n < 1 || enc->k < 1) return fail(MUSE_ERR_INVALID, "proj_12b_tiles: non-positive size");
+  if (!aligned16(x) || !aligned16(tiles12) || (reinterpret_cast<uintptr_t>(y) & 1u))
+    return fail(MUSE_ERR_ALIGN, "proj_12b_tiles: x and tiles 16-byte aligned, y 2-byte aligned");
+  if (plan->kernel != MUSE_KERNEL_TC_12B) return fail(MUSE_ERR_PLAN, "proj_12b_tiles: plan kernel must be TC_12B");
+  return run_skinny(true, tiles12, enc, x, y, m, enc->n, enc->k, *plan, scratch, scratch_bytes,
+                    static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

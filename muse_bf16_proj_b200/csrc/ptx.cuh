@@ -130,6 +130,55 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return mbar_wait_slow(b, parity, where, limit_ns);
 }
 
+// Bounded wait that lets the warp sleep: mbarrier.try_wait suspends the thread until the phase
+// completes or a hardware time limit passes, so a waiting warp takes no issue slots from the warps
+// that share its scheduler. For roles that wait long (an epilogue waiting for a whole main loop).
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __noinline__ bool mbar_wait_idle_slow(uint32_t bar, uint32_t parity, uint32_t where,
+                                                 unsigned long long limit_ns) {
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (error_raised()) return false;
+    if (globaltimer() - t0 > limit_ns) {
+      report_error(where);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, uint32_t where,
+                                               unsigned long long limit_ns = kWaitLimitNs) {
+  const uint32_t b = smem_u32(bar);
+  if (mbar_try_wait(b, parity)) return true;
+  return mbar_wait_idle_slow(b, parity, where, limit_ns);
+}
+
+// A position in a `stages`-deep ring: the slot and the parity of its current phase, advanced by
+// increments. Hot loops use this instead of i % stages and i / stages, which for 64-bit or
+// runtime divisors cost tens of dependent instructions in the single issuing lane.
+struct Ring {
+  int slot = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next(int stages) {
+    if (++slot == stages) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 // ---- programmatic dependent launch -------------------------------------------------------------
 
 // Waits until the grids this one depends on (launched before it in the stream) have completed and
@@ -313,6 +362,29 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 64 consecutive FP32 columns of this warp's 32 TMEM lanes (one load, one wait).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, "
+      "%34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, "
+      "%54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+        "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]),
+        "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]),
+        "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]),
+        "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]),
+        "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // ---- tcgen05 across a CTA pair (cta_group::2) -------------------------------------------------
 
 // Both CTAs of the pair, same warp, same shared-memory slot: the same TMEM columns in each.
@@ -377,6 +449,10 @@ __device__ __forceinline__ uint16_t f32_to_bf16(float f) {
   if ((u & 0x7FFFFFFFu) > 0x7F800000u) return static_cast<uint16_t>((u >> 16) | 0x0040u);
   u += 0x7FFFu + ((u >> 16) & 1u);
   return static_cast<uint16_t>(u >> 16);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return static_cast<uint32_t>(f32_to_bf16(lo)) | (static_cast<uint32_t>(f32_to_bf16(hi)) << 16);
 }
 
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {

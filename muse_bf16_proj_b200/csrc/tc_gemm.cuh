@@ -35,10 +35,6 @@ struct GmArgs {
   int trace_cap;
 };
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return static_cast<uint32_t>(f32_to_bf16(lo)) | (static_cast<uint32_t>(f32_to_bf16(hi)) << 16);
-}
-
 __global__ void __launch_bounds__(kGmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const GmArgs a) {
   constexpr uint32_t kIdesc = umma_idesc_bf16(128, kGmBN);

@@ -1,0 +1,416 @@
+// Stream-K tcgen05 projection for few tokens with W as the UMMA's B operand: y[m, n] = sum_k x[m, k] W[n, k].
+//
+// One tcgen05.mma costs about the same issue time whatever its M (64 or 128) and N (16 .. 256), so
+// the rows of W one instruction consumes set how fast a CTA can stream W through the tensor core.
+// Here an instruction is M = 128 token rows (x, the A operand) x N = 256 rows of W (the B operand)
+// x K = 16: 8 KB of W an instruction, twice what W as the A operand (128 rows) moves.
+//
+// Only the first BNT rows of the A tile are tokens; the MMA reads its other rows from whatever
+// shared memory follows (in bounds: every A window ends inside this CTA's allocation), and their
+// accumulator rows are never read.
+//
+// Work split: units u = (token tile tt, 256-row pair rp, k block kb), kb fastest; CTA c of G takes
+// [c U / G, (c + 1) U / G), one wave. A segment (a run's piece inside one output tile) covering
+// the whole tile stores BF16; otherwise it writes an FP32 partial of its valid token rows to
+// caller scratch and the last contributor (ticket) sums them in contributor order.
+//
+// W sources: kTwelve = false: the packed BF16 tiles (two 16 KB tiles of 128 rows, copied to one
+// 32 KB B tile); kTwelve = true: the 12-bit blocks of tc12.cuh (two 12416-byte blocks a unit),
+// decoded by eight decoder warps (thread r = row r of the 256) into a 32 KB B tile.
+//
+// Warps: 0 producer (lane 0), 1 TMEM owner + UMMA issuer (lane 0), 2..5 epilogue (TMEM lane
+// quarter = warp % 4), 6..13 decoders (kTwelve only).
+#pragma once
+
+#include "ptx.cuh"
+#include "tc12.cuh"
+
+namespace muse {
+
+constexpr int kSnRows = 256;     // W rows a unit (the UMMA's N)
+constexpr int kSnBTile = 32768;  // 256 x 64 BF16, 128-byte swizzled
+constexpr int kSnAWindow = 16384;  // the 128-row A window the MMA reads from an x stage
+
+__host__ __device__ constexpr int sn_threads(bool twelve) { return twelve ? 448 : 192; }
+__host__ __device__ constexpr int sn_xbytes(int bnt) { return bnt * 128; }
+__host__ __device__ constexpr int sn_wbytes(bool twelve) { return twelve ? 2 * kT12Block : kSnBTile; }
+// Layout: x ring | (12-bit: decoded ring) | W ring | barriers. The ring after the x ring is at
+// least 32 KB, so the last x stage's 16 KB A window stays inside the allocation.
+__host__ __device__ constexpr int sn_smem(bool twelve, int bnt, int stages, int dstages) {
+  return 1024 + stages * sn_xbytes(bnt) + (twelve ? dstages * kSnBTile : 0) + stages * sn_wbytes(twelve) +
+         (4 * stages + 2 * dstages + 4) * 8 + 16;
+}
+
+struct SnArgs {
+  const uint8_t* w;         // packed BF16 tiles [rtiles][nkb][16 KB] or 12-bit blocks [rtiles][nkb][12416]
+  const int32_t* esc_ptr;   // 12-bit: per-row escape list (slow path)
+  const uint32_t* esc_val;
+  uint16_t* y;              // [M, N]
+  float* partials;          // [tiles][smax][BNT][256]
+  int* counters;            // [tiles], zero between launches
+  int M, N, stages, dstages;
+  int rtiles, rpairs, nkb, ttiles;
+  long long units;
+  int smax;
+  int y_vec;                // y rows 16-byte aligned (N % 8 == 0 and y aligned): vector stores
+  TraceRec* trace;
+  int trace_cap;
+};
+
+template <bool kTwelve, int BNT>
+__global__ void __launch_bounds__(sn_threads(kTwelve), 1)
+    tc_skinny_kernel(const __grid_constant__ CUtensorMap tmx, const SnArgs a) {
+  constexpr int kX = sn_xbytes(BNT);
+  constexpr int kW = sn_wbytes(kTwelve);
+  constexpr int kBlk = kTwelve ? kT12Block : 16384;  // one 128-row block of a unit
+  constexpr uint32_t kIdesc = umma_idesc_bf16(128, kSnRows);
+  constexpr uint32_t kCols = 512;  // two 256-column accumulators
+  constexpr int kDecWarps = kTwelve ? 8 : 0;
+  extern __shared__ uint8_t smem_raw[];
+  const bool tracing = a.trace != nullptr && static_cast<int>(blockIdx.x) < a.trace_cap && threadIdx.x == 64;
+  const unsigned long long t_start = tracing ? globaltimer() : 0ull;
+  unsigned long long t_ready = 0ull, t_main = 0ull;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stages = a.stages, dstages = kTwelve ? a.dstages : 0;
+  uint8_t* sx = smem;                                               // [stages][BNT x 64 BF16]
+  uint8_t* sdec = sx + static_cast<size_t>(stages) * kX;            // [dstages][32 KB] (12-bit)
+  uint8_t* sw = sdec + static_cast<size_t>(dstages) * kSnBTile;     // [stages][kW]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sw + static_cast<size_t>(stages) * kW);
+  uint64_t* empty = full + stages;                 // W slot free: UMMA commit (BF16) or the decoder warps (12-bit)
+  uint64_t* xempty = empty + stages;               // 12-bit: x slot free (UMMA commit)
+  uint64_t* dec_full = xempty + stages;            // [dstages] decoder warps
+  uint64_t* dec_empty = dec_full + dstages;        // [dstages] UMMA commit
+  uint64_t* acc_full = dec_empty + dstages;        // [2]
+  uint64_t* acc_empty = acc_full + 2;              // [2] epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = gridDim.x;
+  const int c = blockIdx.x;
+  const long long u0 = t12_start(c, a.units, g), u1 = t12_start(c + 1, a.units, g);
+  const int n_units = static_cast<int>(u1 - u0);
+  const int nkb = a.nkb;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmx);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kTwelve ? kDecWarps : 1);
+      mbar_init(&xempty[s], 1);
+    }
+    for (int d = 0; d < dstages; ++d) {
+      mbar_init(&dec_full[d], kDecWarps);
+      mbar_init(&dec_empty[d], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (tracing) t_ready = globaltimer();
+
+  // Unit coordinates, advanced kb, then rp, then tt.
+  struct Pos {
+    int kb, rp, tt;
+  };
+  auto step = [&](Pos& p) {
+    if (++p.kb == nkb) {
+      p.kb = 0;
+      if (++p.rp == a.rpairs) {
+        p.rp = 0;
+        ++p.tt;
+      }
+    }
+  };
+  Pos p0;
+  p0.kb = static_cast<int>(u0 % nkb);
+  p0.rp = static_cast<int>((u0 / nkb) % a.rpairs);
+  p0.tt = static_cast<int>(u0 / nkb / a.rpairs);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      // The unit's W blocks: (2 rp, kb) and, when it exists, (2 rp + 1, kb).
+      auto issue_w = [&](const Pos& p, int s) {
+        const int rt = 2 * p.rp;
+        const int nblk = rt + 1 < a.rtiles ? 2 : 1;
+        mbar_expect_tx(&full[s], static_cast<uint32_t>(nblk * kBlk + kX));
+        const uint8_t* src = a.w + (static_cast<size_t>(rt) * nkb + p.kb) * kBlk;
+        uint8_t* dst = sw + static_cast<size_t>(s) * kW;
+        bulk_g2s(dst, src, kBlk, &full[s], pol_w);
+        if (nblk == 2) bulk_g2s(dst + kBlk, src + static_cast<size_t>(nkb) * kBlk, kBlk, &full[s], pol_w);
+      };
+      const int pre = n_units < stages ? n_units : stages;
+      Pos q = p0;
+      for (int i = 0; i < pre; ++i, step(q)) issue_w(q, i);  // weights first: never the previous grid's output
+      pdl_wait();  // x may be the previous grid's output
+      Ring ring;
+      Pos p = p0;
+      int issued = 0;
+      for (int i = 0; i < n_units; ++i, ring.next(stages), step(p)) {
+        const int s = ring.slot;
+        if (i >= pre) {
+          // 12-bit: the decoders free the W block as soon as they have read it; the x tile of the
+          // same slot is free once the UMMA that read it has completed.
+          if (!mbar_wait(&empty[s], ring.phase ^ 1u, kErrTcProducer)) break;
+          if (kTwelve && !mbar_wait(&xempty[s], ring.phase ^ 1u, kErrTcProducer)) break;
+          issue_w(p, s);
+        }
+        tma_load_2d(sx + static_cast<size_t>(s) * kX, &tmx, &full[s], p.kb * 64, p.tt * BNT, pol_x);
+        ++issued;
+      }
+      for (int i = (issued > stages ? issued - stages : 0); i < issued; ++i)
+        mbar_wait(&full[i % stages], static_cast<uint32_t>((i / stages) & 1), kErrDrain, kWaitLimitNs / 10);
+    }
+    pdl_launch_dependents();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int kb = p0.kb;
+      int seg = 0;
+      Ring rs, rd;
+      for (int i = 0; i < n_units;) {
+        const int b = seg & 1;
+        if (!mbar_wait(&acc_empty[b], static_cast<uint32_t>((seg >> 1) & 1) ^ 1u, kErrTcMma)) {
+          umma_commit(&acc_full[b]);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + static_cast<uint32_t>(b * kSnRows);
+        bool ok = true, first = true;
+        for (; i < n_units; ++i) {  // one segment: until this output tile's k blocks end
+          if ((kTwelve && !mbar_wait(&dec_full[rd.slot], rd.phase, kErrTcMma)) ||
+              !mbar_wait(&full[rs.slot], rs.phase, kErrTcMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = umma_desc_sw128(smem_u32(sx + static_cast<size_t>(rs.slot) * kX));
+          const uint64_t db = umma_desc_sw128(
+              smem_u32(kTwelve ? sdec + static_cast<size_t>(rd.slot) * kSnBTile : sw + static_cast<size_t>(rs.slot) * kW));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) umma_bf16(acc, da + 2 * kk, db + 2 * kk, kIdesc, (first && kk == 0) ? 0u : 1u);
+          first = false;
+          if (kTwelve) {
+            umma_commit(&dec_empty[rd.slot]);
+            rd.next(dstages);
+          }
+          umma_commit(kTwelve ? &xempty[rs.slot] : &empty[rs.slot]);
+          rs.next(stages);
+          if (++kb == nkb) {
+            kb = 0;
+            ++i;
+            break;
+          }
+        }
+        umma_commit(&acc_full[b]);  // also on the error path, so the epilogue's wait ends
+        ++seg;
+        if (!ok) break;
+      }
+    }
+    pdl_launch_dependents();
+  } else if (kTwelve && warp >= 6) {
+    // Decoders: thread r = row r of the unit's 256 rows (block h = r / 128, its row r % 128).
+    const int r = (warp - 6) * 32 + lane;
+    const int h = r >> 7, rb = r & 127, swz = r & 7;
+    Ring rs, rd;
+    Pos p = p0;
+    for (int i = 0; i < n_units; ++i, rs.next(stages), rd.next(dstages), step(p)) {
+      const int s = rs.slot, d = rd.slot;
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], rs.phase, kErrTcEpilogue));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&dec_empty[d], rd.phase ^ 1u, kErrTcEpilogue));
+      if (!ok) break;
+      const int rt = 2 * p.rp + h;
+      if (rt < a.rtiles) {  // warp-uniform: a warp's rows are in one block
+        const uint8_t* blk = sw + static_cast<size_t>(s) * kW + h * kT12Block;
+        const uint32_t* area = reinterpret_cast<const uint32_t*>(blk + kT12Raw);
+        const uint4 l0 = *reinterpret_cast<const uint4*>(blk + rb * 16);
+        const uint4 l1 = *reinterpret_cast<const uint4*>(blk + 2048 + rb * 16);
+        const uint4 l2 = *reinterpret_cast<const uint4*>(blk + 4096 + rb * 16);
+        const uint4 l3 = *reinterpret_cast<const uint4*>(blk + 6144 + rb * 16);
+        const uint4 c0 = *reinterpret_cast<const uint4*>(blk + 8192 + rb * 16);
+        const uint4 c1 = *reinterpret_cast<const uint4*>(blk + 10240 + rb * 16);
+        const uint32_t head = area[0];
+        const uint32_t base4 = (head >> 16) * 0x01010101u;
+        const uint32_t l03 = base4 + 0x03020100u, l47 = base4 + 0x07060504u;
+        const int n_esc = static_cast<int>(head & 0xFFFFu);
+        uint8_t* drow = sdec + static_cast<size_t>(d) * kSnBTile + r * 128;
+        *reinterpret_cast<uint4*>(drow + ((0 ^ swz) << 4)) = decode12_bf16x8(l0.x, l0.y, c0.x, l03, l47);
+        *reinterpret_cast<uint4*>(drow + ((1 ^ swz) << 4)) = decode12_bf16x8(l0.z, l0.w, c0.y, l03, l47);
+        *reinterpret_cast<uint4*>(drow + ((2 ^ swz) << 4)) = decode12_bf16x8(l1.x, l1.y, c0.z, l03, l47);
+        *reinterpret_cast<uint4*>(drow + ((3 ^ swz) << 4)) = decode12_bf16x8(l1.z, l1.w, c0.w, l03, l47);
+        *reinterpret_cast<uint4*>(drow + ((4 ^ swz) << 4)) = decode12_bf16x8(l2.x, l2.y, c1.x, l03, l47);
+        *reinterpret_cast<uint4*>(drow + ((5 ^ swz) << 4)) = decode12_bf16x8(l2.z, l2.w, c1.y, l03, l47);
+        *reinterpret_cast<uint4*>(drow + ((6 ^ swz) << 4)) = decode12_bf16x8(l3.x, l3.y, c1.z, l03, l47);
+        *reinterpret_cast<uint4*>(drow + ((7 ^ swz) << 4)) = decode12_bf16x8(l3.z, l3.w, c1.w, l03, l47);
+        if (n_esc <= kT12EscSlots) {
+          for (int j = 1; j <= n_esc; ++j) {  // the same word across the warp: broadcast reads
+            const uint32_t e = area[j];
+            if (static_cast<int>(e >> 22) == rb) t12_patch(drow, swz, static_cast<int>((e >> 16) & 63u), e);
+          }
+        } else {
+          const int row = rt * 128 + rb;  // escape-dense block: the row's list
+          if (row < a.N) {
+            const int hi = __ldg(a.esc_ptr + row + 1);
+            for (int e = t12_lower_bound(a.esc_val, __ldg(a.esc_ptr + row), hi, static_cast<uint32_t>(p.kb * 64));
+                 e < hi; ++e) {
+              const uint32_t v = __ldg(a.esc_val + e);
+              const int kk = static_cast<int>(v >> 16) - p.kb * 64;
+              if (kk >= 64) break;
+              t12_patch(drow, swz, kk, v);
+            }
+          }
+        }
+        fence_proxy_async_smem();  // the tensor cores read this tile through the async proxy
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&dec_full[d]);
+        mbar_arrive(&empty[s]);
+      }
+    }
+  } else if (warp >= 2 && warp <= 5) {
+    // Epilogue: TMEM lane = token row of the tile, columns = the unit's 256 W rows.
+    const int q = warp & 3;
+    const int t = (warp - 2) * 32 + lane;  // 0..127: reduction / store index
+    int seg = 0;
+    bool waited = false;
+    for (long long u = u0; u < u1; ++seg) {
+      const long long tile = u / nkb;
+      const long long seg_end = min(u1, (tile + 1) * nkb);
+      const bool whole = (u == tile * nkb) && (seg_end == (tile + 1) * nkb);
+      const int b = seg & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait_idle(&acc_full[b], static_cast<uint32_t>((seg >> 1) & 1),
+                                                             kErrTcEpilogue));
+      tc_fence_after();
+      if (!waited) {
+        if (tracing) t_main = globaltimer();
+        pdl_launch_dependents();
+        pdl_wait();  // y and the counters may still be in use by the previous grid
+        waited = true;
+      }
+      const int tt = static_cast<int>(tile / a.rpairs);
+      const int rp = static_cast<int>(tile % a.rpairs);
+      const int n0 = rp * kSnRows;
+      const int mvalid = min(BNT, a.M - tt * BNT);  // token rows of this tile
+      const int ml = q * 32 + lane;                  // this thread's TMEM lane = token row
+      int first_c = c, nseg = 1;
+      float* slots = nullptr;
+      if (!whole) {
+        first_c = t12_owner(tile * nkb, a.units, g);
+        nseg = t12_owner((tile + 1) * nkb - 1, a.units, g) - first_c + 1;
+        slots = a.partials + static_cast<size_t>(tile) * a.smax * (BNT * kSnRows);
+      }
+      if (ok && q * 32 < mvalid) {  // warp-uniform: lane quarters holding token rows
+        const int m = tt * BNT + ml;
+        const bool mine = ml < mvalid;
+        float* slot = whole ? nullptr : slots + (static_cast<size_t>(c - first_c) * BNT + ml) * kSnRows;
+#pragma unroll 1
+        for (int c64 = 0; c64 < kSnRows; c64 += 64) {
+          float v[64];
+          tmem_ld64(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kSnRows + c64), v);
+          if (!mine) continue;
+          if (whole) {
+            const int n = n0 + c64;
+            uint16_t* dst = a.y + static_cast<size_t>(m) * a.N + n;
+            if (a.y_vec && n + 64 <= a.N) {
+#pragma unroll
+              for (int j = 0; j < 64; j += 8)
+                *reinterpret_cast<uint4*>(dst + j) = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                                                                pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 64; ++j)
+                if (n + j < a.N) dst[j] = f32_to_bf16(v[j]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 64; j += 4)
+              __stcg(reinterpret_cast<float4*>(slot + c64 + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (!whole) {
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // every partial store of this CTA precedes the ticket
+        if (t == 0) *last_flag = (ticket_acq_rel(a.counters + tile) == nseg - 1) ? 1 : 0;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (*last_flag) {
+          // Sum the contributors' partials in contributor order (deterministic). The tile's valid
+          // rows are float4 groups g = row * 64 + col / 4; thread t takes groups t, t + 128, ...,
+          // kB at a time with their loads issued together.
+          constexpr int kB = 8;
+          const int groups = mvalid * (kSnRows / 4);
+          const float4* part = reinterpret_cast<const float4*>(slots);
+          const size_t cstride = static_cast<size_t>(BNT) * (kSnRows / 4);  // float4s between contributors
+#pragma unroll 1
+          for (int g0 = t; g0 < groups; g0 += 128 * kB) {
+            float4 acc[kB];
+#pragma unroll
+            for (int j = 0; j < kB; ++j) {
+              const int gi = g0 + j * 128;
+              acc[j] = gi < groups ? __ldcg(part + gi) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll 1
+            for (int k2 = 1; k2 < nseg; ++k2) {
+              float4 v[kB];
+#pragma unroll
+              for (int j = 0; j < kB; ++j) {
+                const int gi = g0 + j * 128;
+                v[j] = gi < groups ? __ldcg(part + k2 * cstride + gi) : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int j = 0; j < kB; ++j) {
+                acc[j].x += v[j].x;
+                acc[j].y += v[j].y;
+                acc[j].z += v[j].z;
+                acc[j].w += v[j].w;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < kB; ++j) {
+              const int gi = g0 + j * 128;
+              if (gi >= groups) continue;
+              const int n = n0 + (gi & 63) * 4;
+              uint16_t* dst = a.y + static_cast<size_t>(tt * BNT + (gi >> 6)) * a.N + n;
+              if (a.y_vec && n + 4 <= a.N) {
+                *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(acc[j].x, acc[j].y), pack_bf16x2(acc[j].z, acc[j].w));
+              } else {
+                const float e[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
+                for (int i = 0; i < 4; ++i)
+                  if (n + i < a.N) dst[i] = f32_to_bf16(e[i]);
+              }
+            }
+          }
+          if (t == 0) a.counters[tile] = 0;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // last_flag is reused by the next segment
+      }
+      u = seg_end;
+    }
+    if (!waited) {
+      pdl_launch_dependents();
+      pdl_wait();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+  if (tracing) a.trace[blockIdx.x] = TraceRec{t_start, t_ready, t_main, globaltimer(), smid(), blockIdx.x, 0u, 0u};
+}
+
+}  // namespace muse

@@ -75,6 +75,9 @@ class _Enc12Device:
         self.escape_fraction = enc.escape_fraction
         self._esc_ptr_host = enc.esc_ptr
         self._views: dict = {}
+        # The same weights re-laid in 12 KB blocks of 128 rows x 64 k for the tensor-core kernel.
+        self.tiles12 = torch.empty(_lib.tiles12_bytes(enc.n, enc.k), dtype=torch.uint8, device=device)
+        _lib.pack_tiles12(self.view(enc.n), self.tiles12.data_ptr(), torch.cuda.current_stream(device).cuda_stream)
 
     def view(self, n: int) -> _lib.MuseEnc12:
         v = self._views.get(n)
@@ -86,7 +89,8 @@ class _Enc12Device:
 
     @property
     def nbytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in (self.planes, self.bases, self.esc_ptr, self.esc_val))
+        return sum(t.numel() * t.element_size() for t in (self.planes, self.tiles12, self.bases, self.esc_ptr,
+                                                          self.esc_val))
 
 
 def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | None = None,
@@ -200,7 +204,12 @@ def project(x: torch.Tensor, state: dict, layer: str, n: int | None = None,
                                                                                 "flags": plan.flags | _lib.FLAG_PDL}))
     y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     stream = torch.cuda.current_stream(x.device).cuda_stream
-    if fmt == "12b":
+    if fmt == "12b" and plan.kernel == _lib.KERNEL_TC_12B:
+        scratch = _scratch_for(state, m, n, k, plan)
+        _lib.proj_12b_tiles(enc.view(n), enc.tiles12.data_ptr(), x.data_ptr(), y.data_ptr(), m, plan, stream,
+                            scratch.data_ptr() if scratch is not None else 0,
+                            scratch.numel() if scratch is not None else 0)
+    elif fmt == "12b":
         _lib.proj_12b(enc.view(n), x.data_ptr(), y.data_ptr(), m, plan, stream)
     elif plan.kernel in _lib.TILE_KERNELS and layer in state["tiles"]:
         scratch = _scratch_for(state, m, n, k, plan)

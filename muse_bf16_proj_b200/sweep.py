@@ -46,6 +46,15 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
     if twelve_ok and m <= 4:
         for warps, ctas in ((8, 2 * sms), (16, sms), (16, 2 * sms)):
             out.append(("12b", _lib.MusePlan(kernel=_lib.KERNEL_GEMV_12B, warps=warps, ctas=ctas)))
+    b16 = 16
+    while b16 < m and b16 < 128:
+        b16 *= 2
+    if twelve_ok and k % 512 == 0 and m <= 256:
+        for stages, dst in ((0, 2), (5, 2), (4, 3)):
+            out.append(("12b", _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, tile_n=b16, ctas=sms, stages=stages, chunk=dst)))
+    if m <= 256:
+        for stages in (0, 4, 6):
+            out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_SKINNY, tile_n=b16, ctas=sms, stages=stages)))
     bnt = 16
     while bnt < m and bnt < 256:
         bnt *= 2
@@ -104,7 +113,10 @@ class ShapeBench:
     def launch(self, i: int, m: int, fmt: str, plan: _lib.MusePlan) -> None:
         j = i % self.rot
         st = torch.cuda.current_stream().cuda_stream
-        if fmt == "12b":
+        if fmt == "12b" and plan.kernel == _lib.KERNEL_TC_12B:
+            _lib.proj_12b_tiles(self.enc[j].view(self.n), self.enc[j].tiles12.data_ptr(), self.x[j].data_ptr(),
+                                self.y[j].data_ptr(), m, plan, st, self.scratch.data_ptr(), self.scratch.numel())
+        elif fmt == "12b":
             _lib.proj_12b(self.enc[j].view(self.n), self.x[j].data_ptr(), self.y[j].data_ptr(), m, plan, st)
         elif plan.kernel in _lib.TILE_KERNELS:
             _lib.proj_bf16_tiles(self.x[j].data_ptr(), self.tiles[j].data_ptr(), self.y[j].data_ptr(), m, self.n,
@@ -287,7 +299,7 @@ def main():
     only = None
     if args.plan:
         d = json.loads(args.plan)
-        only = [("12b" if d.get("kernel") == "gemv_12b" else "bf16", _lib.MusePlan.from_dict(d))]
+        only = [("12b" if d.get("kernel") in ("gemv_12b", "tc_12b") else "bf16", _lib.MusePlan.from_dict(d))]
     shapes = []
     for s in args.shapes.split(","):
         if s == "reference":

@@ -43,6 +43,15 @@ def test_proj_argument_errors_before_any_device_work():
     enc_bad = _lib.MuseEnc12(None, 16, 16, 16, 128, 512, 0)
     assert lib.muse_proj_12b(ctypes.byref(enc_bad), 16, 16, 1, ctypes.byref(plan12), None) == -1
     assert b"null" in lib.muse_last_error()
+    # 12-bit tiles: sizes, K rules, null and plan checks
+    assert lib.muse_tiles12_bytes(200, 1024, ctypes.byref(b)) == 0 and b.value == 2 * 16 * 12416
+    assert lib.muse_tiles12_bytes(200, 1000, ctypes.byref(b)) == -3
+    assert lib.muse_pack_tiles12(ctypes.byref(enc_bad), 16, None) == -1
+    assert lib.muse_pack_tiles12(ctypes.byref(enc), 18, None) == -2
+    t12 = _lib.MusePlan(kernel=_lib.KERNEL_TC_12B)
+    assert lib.muse_proj_12b_tiles(ctypes.byref(enc), None, 16, 16, 1, ctypes.byref(t12), None, 0, None) == -1
+    assert lib.muse_proj_12b_tiles(ctypes.byref(enc), 16, 18, 16, 1, ctypes.byref(t12), None, 0, None) == -2
+    assert lib.muse_proj_12b_tiles(ctypes.byref(enc), 16, 16, 16, 1, ctypes.byref(plan12), None, 0, None) == -7
 
 
 def test_plan_default_without_device():
@@ -60,6 +69,12 @@ def test_plan_default_without_device():
         _lib.plan_default(4096, 10240, 8192)  # needs packed tiles
     p = _lib.plan_default(1, 10240, 8192, weights_12b=True)
     assert p.kernel == _lib.KERNEL_GEMV_12B
+    p = _lib.plan_default(1, 10240, 8192, weights_12b=True, tiles=True)
+    assert p.kernel == _lib.KERNEL_TC_12B and p.tile_n == 16 and p.ctas > 0 and p.chunk == 2
+    p = _lib.plan_default(300, 2304, 8192, weights_12b=True, tiles=True)
+    assert p.kernel == _lib.KERNEL_TC_12B and p.tile_n == 128
+    with pytest.raises(_lib.MuseError):
+        _lib.plan_default(1, 2304, 1000, weights_12b=True, tiles=True)
     with pytest.raises(_lib.MuseError):
         _lib.plan_default(0, 10, 10)
 

@@ -341,6 +341,29 @@ def test_tc_streamk(m, n, k, tile_n, stages, ctas):
     assert int(torch.count_nonzero(scratch_buf()[: 64 * 1024])) == 0, "stream-K counters not back at 0"
 
 
+SN_CASES = [  # (m, n, k, tile_n, stages, ctas)
+    (16, 6144, 4096, 16, 5, 0), (1, 6144, 4096, 16, 0, 0), (1, 10240, 8192, 16, 6, 148),
+    (8, 2304, 8192, 16, 4, 148), (5, 1024, 4096, 16, 3, 0), (32, 4096, 8192, 32, 5, 0),
+    (33, 8192, 1024, 64, 4, 0), (64, 640, 2048, 64, 5, 7), (100, 1001, 1000, 128, 3, 50),
+    (130, 384, 512, 128, 4, 0), (256, 2304, 8192, 128, 2, 0), (7, 200, 4096, 16, 5, 1000),
+    (16, 128, 64, 16, 2, 0), (3, 136, 4096, 16, 5, 9),
+]
+
+
+@pytest.mark.parametrize("m,n,k,tile_n,stages,ctas", SN_CASES)
+def test_tc_skinny(m, n, k, tile_n, stages, ctas):
+    """W as the B operand (256 W rows an MMA), stream-K: odd row-tile counts, ragged K and N,
+    several token tiles, grids larger than the unit count."""
+    xb, wb = _rand_bits((m, k), 90 + m), _rand_bits((n, k), 95 + n, 0.02)
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_SKINNY, tile_n=tile_n, stages=stages, ctas=ctas)
+    assert _lib.scratch_bytes(m, n, k, plan) <= scratch_buf().numel()
+    y = _run_bf16(xb, wb, plan, tiles=True)
+    assert_parity(xb, wb, y, what=f"skinny m={m} n={n} k={k} tile={tile_n} stages={stages} ctas={ctas}")
+    y2 = _run_bf16(xb, wb, plan, tiles=True)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16)), "skinny reduction is not deterministic"
+    assert int(torch.count_nonzero(scratch_buf()[: 64 * 1024])) == 0, "skinny counters not back at 0"
+
+
 def test_tc_streamk_needs_scratch():
     x = torch.zeros((4, 1024), dtype=torch.bfloat16, device="cuda")
     t = torch.zeros(_lib.tiles_bytes(256, 1024), dtype=torch.uint8, device="cuda")
