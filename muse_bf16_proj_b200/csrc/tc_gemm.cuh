@@ -80,7 +80,8 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     if (lane == 0) {
       const uint64_t pol_keep = policy_evict_last();  // both operands are re-read by other tiles
       pdl_wait();
-      long long it = 0;  // k blocks issued by this CTA so far (ring position)
+      Ring ring;     // ring position of the next k block
+      int issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         const int mt = t % a.mtiles, nt = t / a.mtiles;
@@ -88,9 +89,9 @@ __global__ void __launch_bounds__(kGmThreads, 1)
         const int rt1 = rt0 + 1 < a.rtiles ? rt0 + 1 : rt0;  // past N: reload a valid tile, rows are masked
         const uint8_t* w0 = a.wtiles + static_cast<size_t>(rt0) * nkb * 16384;
         const uint8_t* w1 = a.wtiles + static_cast<size_t>(rt1) * nkb * 16384;
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = static_cast<int>(it % stages);
-          if (!mbar_wait(&empty[s], static_cast<uint32_t>((it / stages) & 1) ^ 1u, kErrTcProducer)) {
+        for (int kb = 0; kb < nkb; ++kb, ++issued, ring.next(stages)) {
+          const int s = ring.slot;
+          if (!mbar_wait(&empty[s], ring.phase ^ 1u, kErrTcProducer)) {
             ok = false;
             break;
           }
@@ -101,13 +102,12 @@ __global__ void __launch_bounds__(kGmThreads, 1)
           bulk_g2s(bdst + 16384, w1 + static_cast<size_t>(kb) * 16384, 16384, &full[s], pol_keep);
         }
       }
-      const long long issued = it;
-      for (long long i = (issued > stages ? issued - stages : 0); i < issued; ++i)
+      for (int i = (issued > stages ? issued - stages : 0); i < issued; ++i)
         mbar_wait(&full[i % stages], static_cast<uint32_t>((i / stages) & 1), kErrDrain, kWaitLimitNs / 10);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      long long it = 0;
+      Ring ring;
       int local = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++local) {
@@ -115,9 +115,9 @@ __global__ void __launch_bounds__(kGmThreads, 1)
         ok = mbar_wait(&acc_empty[b], static_cast<uint32_t>((local >> 1) & 1) ^ 1u, kErrTcMma);
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(b * kGmBN);
-        for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
-          const int s = static_cast<int>(it % stages);
-          if (!mbar_wait(&full[s], static_cast<uint32_t>((it / stages) & 1), kErrTcMma)) {
+        for (int kb = 0; kb < nkb && ok; ++kb, ring.next(stages)) {
+          const int s = ring.slot;
+          if (!mbar_wait(&full[s], ring.phase, kErrTcMma)) {
             ok = false;
             break;
           }

@@ -87,16 +87,17 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     if (lane == 0) {
       const uint64_t pol = policy_evict_last();  // x and W tiles are re-read by other pairs
       pdl_wait();
-      long long it = 0;
+      Ring ring;     // ring position of the next k block
+      int issued = 0;
       bool ok = true;
       for (int t = pair; t < tiles && ok; t += npairs) {
         const int mt = t % a.mtiles, nt = t / a.mtiles;
         const int xrow = mt * 256 + static_cast<int>(rank) * 128;
         int rt = nt * 2 + static_cast<int>(rank);
         if (rt >= a.rtiles) rt = nt * 2;  // past N: a valid tile; its rows are never stored
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = static_cast<int>(it % stages);
-          if (!mbar_wait(&empty[s], static_cast<uint32_t>((it / stages) & 1) ^ 1u, kErrTcProducer)) {
+        for (int kb = 0; kb < nkb; ++kb, ++issued, ring.next(stages)) {
+          const int s = ring.slot;
+          if (!mbar_wait(&empty[s], ring.phase ^ 1u, kErrTcProducer)) {
             ok = false;
             break;
           }
@@ -107,13 +108,12 @@ __global__ void __launch_bounds__(kG2Threads, 1)
         }
       }
       // Every load this CTA issued is consumed (and so has landed) once its stage is released.
-      const long long issued = it;
-      for (long long i = (issued > stages ? issued - stages : 0); i < issued; ++i)
+      for (int i = (issued > stages ? issued - stages : 0); i < issued; ++i)
         mbar_wait(&empty[i % stages], static_cast<uint32_t>((i / stages) & 1), kErrDrain, kWaitLimitNs / 10);
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      long long it = 0;
+      Ring ring;
       int local = 0;
       bool ok = true;
       for (int t = pair; t < tiles && ok; t += npairs, ++local) {
@@ -121,9 +121,9 @@ __global__ void __launch_bounds__(kG2Threads, 1)
         ok = mbar_wait(&acc_empty[b], static_cast<uint32_t>((local >> 1) & 1) ^ 1u, kErrTcMma);
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(b * 256);
-        for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
-          const int s = static_cast<int>(it % stages);
-          if (!mbar_wait(&full[s], static_cast<uint32_t>((it / stages) & 1), kErrTcMma)) {
+        for (int kb = 0; kb < nkb && ok; ++kb, ring.next(stages)) {
+          const int s = ring.slot;
+          if (!mbar_wait(&full[s], ring.phase, kErrTcMma)) {
             ok = false;
             break;
           }

@@ -105,70 +105,94 @@ __global__ void __launch_bounds__(kSkThreads, 2)
   const uint32_t tmem = *tmem_slot;
   if (tracing) t_ready = globaltimer();
 
+  // Unit coordinates of u0, advanced kb, then rt, then tt (no division in the loops).
+  struct Pos {
+    int kb, rt, tt;
+  };
+  auto step = [&](Pos& p) {
+    if (++p.kb == nkb) {
+      p.kb = 0;
+      if (++p.rt == a.rtiles) {
+        p.rt = 0;
+        ++p.tt;
+      }
+    }
+  };
+  Pos p0;
+  p0.kb = static_cast<int>(u0 % nkb);
+  p0.rt = static_cast<int>((u0 / nkb) % a.rtiles);
+  p0.tt = static_cast<int>(u0 / nkb / a.rtiles);
+  const int n_units = static_cast<int>(u1 - u0);
+
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
-      auto w_src = [&](long long u) {
-        const long long tile = u / nkb;  // (tt, rt)
-        const long long rt = tile % a.rtiles;
-        return a.wtiles + (static_cast<size_t>(rt) * nkb + static_cast<size_t>(u % nkb)) * kABytes;
+      auto w_src = [&](const Pos& p) {
+        return a.wtiles + (static_cast<size_t>(p.rt) * nkb + static_cast<size_t>(p.kb)) * kABytes;
       };
-      auto x_load = [&](long long u, int s) {
-        const int tt = static_cast<int>(u / nkb / a.rtiles);
-        tma_load_2d(sb + static_cast<size_t>(s) * kBBytes, &tmx, &full[s], static_cast<int>(u % nkb) * 64,
-                    tt * BNT, pol_x);
-      };
-      const long long n = u1 - u0;
-      const int pre = static_cast<int>(n < stages ? n : stages);
-      for (int i = 0; i < pre; ++i) {
+      const int pre = n_units < stages ? n_units : stages;
+      Pos q = p0;
+      for (int i = 0; i < pre; ++i, step(q)) {
         mbar_expect_tx(&full[i], static_cast<uint32_t>(kABytes + kBBytes));
-        bulk_g2s(sa + static_cast<size_t>(i) * kABytes, w_src(u0 + i), kABytes, &full[i], pol_w);
+        bulk_g2s(sa + static_cast<size_t>(i) * kABytes, w_src(q), kABytes, &full[i], pol_w);
       }
       pdl_wait();  // x may be the previous grid's output
-      for (int i = 0; i < pre; ++i) x_load(u0 + i, i);
-      long long issued = pre;
-      for (long long i = pre; i < n; ++i) {
-        const int s = static_cast<int>(i % stages);
-        if (!mbar_wait(&empty[s], static_cast<uint32_t>((i / stages) & 1) ^ 1u, kErrTcProducer)) break;
-        mbar_expect_tx(&full[s], static_cast<uint32_t>(kABytes + kBBytes));
-        bulk_g2s(sa + static_cast<size_t>(s) * kABytes, w_src(u0 + i), kABytes, &full[s], pol_w);
-        x_load(u0 + i, s);
+      Ring ring;
+      Pos p = p0;
+      int issued = 0;
+      for (int i = 0; i < n_units; ++i, ring.next(stages), step(p)) {
+        const int s = ring.slot;
+        if (i >= pre) {
+          if (!mbar_wait(&empty[s], ring.phase ^ 1u, kErrTcProducer)) break;
+          mbar_expect_tx(&full[s], static_cast<uint32_t>(kABytes + kBBytes));
+          bulk_g2s(sa + static_cast<size_t>(s) * kABytes, w_src(p), kABytes, &full[s], pol_w);
+        }
+        tma_load_2d(sb + static_cast<size_t>(s) * kBBytes, &tmx, &full[s], p.kb * 64, p.tt * BNT, pol_x);
         ++issued;
       }
-      for (long long i = (issued > stages ? issued - stages : 0); i < issued; ++i)
+      for (int i = (issued > stages ? issued - stages : 0); i < issued; ++i)
         mbar_wait(&full[i % stages], static_cast<uint32_t>((i / stages) & 1), kErrDrain, kWaitLimitNs / 10);
     }
     pdl_launch_dependents();
   } else if (warp == 1) {
     if (lane == 0) {
+      int kb = p0.kb;
       int seg = 0;
-      bool ok = true;
-      for (long long u = u0; u < u1 && ok;) {
-        const long long seg_start = u;
-        const long long seg_end = min(u1, (u / nkb + 1) * nkb);
+      Ring ring;
+      for (int i = 0; i < n_units;) {
         const int b = seg & 1;
         // The epilogue must have drained this accumulator (its use seg / 2 - 1).
-        ok = mbar_wait(&acc_empty[b], static_cast<uint32_t>((seg >> 1) & 1) ^ 1u, kErrTcMma);
+        if (!mbar_wait(&acc_empty[b], static_cast<uint32_t>((seg >> 1) & 1) ^ 1u, kErrTcMma)) {
+          umma_commit(&acc_full[b]);
+          break;
+        }
         tc_fence_after();
-        for (; u < seg_end && ok; ++u) {
-          const long long i = u - u0;
-          const int s = static_cast<int>(i % stages);
-          if (!mbar_wait(&full[s], static_cast<uint32_t>((i / stages) & 1), kErrTcMma)) {
+        const uint32_t d = tmem + static_cast<uint32_t>(b * BNT);
+        bool ok = true, first = true;
+        for (; i < n_units; ++i) {  // one segment: until this output tile's k blocks end
+          const int s = ring.slot;
+          if (!mbar_wait(&full[s], ring.phase, kErrTcMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint64_t da = umma_desc_sw128(smem_u32(sa + static_cast<size_t>(s) * kABytes));
           const uint64_t db = umma_desc_sw128(smem_u32(sb + static_cast<size_t>(s) * kBBytes));
-          const uint32_t d = tmem + static_cast<uint32_t>(b * BNT);
-          const bool first = (u == seg_start);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) umma_bf16(d, da + 2 * kk, db + 2 * kk, kIdesc, (first && kk == 0) ? 0u : 1u);
+          first = false;
           umma_commit(&empty[s]);
+          ring.next(stages);
+          if (++kb == nkb) {
+            kb = 0;
+            ++i;
+            break;
+          }
         }
         umma_commit(&acc_full[b]);  // also on the error path, so the epilogue's wait ends
         ++seg;
+        if (!ok) break;
       }
     }
     pdl_launch_dependents();

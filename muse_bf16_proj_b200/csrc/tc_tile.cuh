@@ -144,9 +144,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int i = 0; i < pre; ++i)
         tma_load_2d(sb + static_cast<size_t>(i) * kBBytes, &tmx, &full[i], (kb0 + i) * kTcBK, tt * BNT, pol_x);
       int issued = pre;
-      for (int i = pre; i < nk; ++i) {
-        const int s = i % stages;
-        if (!mbar_wait(&empty[s], ((i / stages) & 1) ^ 1, kErrTcProducer)) break;
+      Ring ring;  // position of unit pre
+      for (int i = 0; i < pre; ++i) ring.next(stages);
+      for (int i = pre; i < nk; ++i, ring.next(stages)) {
+        const int s = ring.slot;
+        if (!mbar_wait(&empty[s], ring.phase ^ 1u, kErrTcProducer)) break;
         mbar_expect_tx(&full[s], static_cast<uint32_t>(kTcABytes + kBBytes));
         load_w(i, s);
         tma_load_2d(sb + static_cast<size_t>(s) * kBBytes, &tmx, &full[s], (kb0 + i) * kTcBK, tt * BNT, pol_x);
@@ -158,9 +160,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_launch_dependents();
   } else if (warp == 1) {
     if (lane == 0) {
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % stages;
-        if (!mbar_wait(&full[s], (i / stages) & 1, kErrTcMma)) break;
+      Ring ring;
+      for (int i = 0; i < nk; ++i, ring.next(stages)) {
+        const int s = ring.slot;
+        if (!mbar_wait(&full[s], ring.phase, kErrTcMma)) break;
         tc_fence_after();
         const uint64_t da = umma_desc_sw128(smem_u32(sa + static_cast<size_t>(s) * kTcABytes));
         const uint64_t db = umma_desc_sw128(smem_u32(sb + static_cast<size_t>(s) * kBBytes));
