@@ -55,7 +55,7 @@ typedef struct MusePlan {
   int32_t stages; /* shared-memory ring depth (0 = kernel default) */
   int32_t ctas;   /* GEMV, TC_STREAMK, TC_SKINNY, TC_12B: CTAs in the grid (0 = one per SM) */
   int32_t warps;  /* GEMV: consumer warps per CTA: 4, 8 or 16 (0 = 8) */
-  int32_t chunk;  /* GEMV: units per bulk copy (0 = about 16 KB); TC_12B: decoded-tile ring depth 1..4 (0 = 2) */
+  int32_t chunk;  /* GEMV: units per bulk copy (0 = about 16 KB) */
   int32_t flags;  /* MUSE_FLAG_* */
 } MusePlan;
 

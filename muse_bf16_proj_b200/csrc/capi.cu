@@ -580,7 +580,7 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
 // ---- stream-K skinny kernel: W as the UMMA's B operand (BF16 tiles or 12-bit blocks) -----------
 
 struct SnShape {
-  int bnt, stages, dstages, g, smax;
+  int bnt, stages, g, smax;
   int rtiles, rpairs, nkb, ttiles;
   long long units, tiles;
   int64_t scratch;
@@ -606,17 +606,14 @@ int sn_shape(bool twelve, int64_t m, int64_t n, int64_t k, const MusePlan& p, Sn
   }
   if (bnt != 16 && bnt != 32 && bnt != 64 && bnt != 128)
     return fail(MUSE_ERR_PLAN, "%s: tile_n must be 16, 32, 64 or 128 (got %d)", name, bnt);
-  const int dstages = twelve ? (p.chunk > 0 ? p.chunk : 2) : 0;
-  if (dstages > 4) return fail(MUSE_ERR_PLAN, "%s: chunk (decoded-tile stages) must be 1..4 (got %d)", name, dstages);
-  const int per_stage = muse::sn_xbytes(bnt) + muse::sn_wbytes(twelve) + 32;
-  const int max_stages = (limit - muse::sn_smem(twelve, bnt, 0, dstages)) / per_stage;
-  const int stages = p.stages > 0 ? p.stages : std::min(twelve ? 6 : 5, max_stages);
+  const int per_stage = muse::sn_smem(bnt, 1) - muse::sn_smem(bnt, 0);
+  const int max_stages = (limit - muse::sn_smem(bnt, 0)) / per_stage;
+  const int stages = p.stages > 0 ? p.stages : std::min(5, max_stages);
   if (stages < 2 || stages > max_stages)
     return fail(MUSE_ERR_PLAN, "%s: %d stages do not fit (max %d)", name, stages, max_stages);
   SnShape sh;
   sh.bnt = bnt;
   sh.stages = stages;
-  sh.dstages = dstages;
   sh.rtiles = static_cast<int>((n + 127) / 128);
   sh.rpairs = (sh.rtiles + 1) / 2;
   sh.nkb = static_cast<int>((k + 63) / 64);
@@ -644,7 +641,7 @@ int launch_sn_t(const CUtensorMap& tmx, const muse::SnArgs& a, int g, bool pdl, 
   auto kern = muse::tc_skinny_kernel<kTwelve, BNT>;
   // Every CTA holds all 512 TMEM columns: ask for more than half an SM's shared memory so that
   // no two CTAs (of this or the next launch) share an SM.
-  const int smem = std::max(muse::sn_smem(kTwelve, BNT, a.stages, a.dstages), 116 * 1024);
+  const int smem = std::max(muse::sn_smem(BNT, a.stages), 116 * 1024);
   static bool configured[kMaxDevices] = {};
   int dev;
   if (int rc = current_device(&dev)) return rc;
@@ -693,7 +690,6 @@ int run_skinny(bool twelve, const void* w, const MuseEnc12* enc, const void* x, 
   a.M = static_cast<int>(m);
   a.N = static_cast<int>(n);
   a.stages = sh.stages;
-  a.dstages = sh.dstages;
   a.rtiles = sh.rtiles;
   a.rpairs = sh.rpairs;
   a.nkb = sh.nkb;
@@ -774,7 +770,6 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
     while (bnt < m && bnt < 128) bnt *= 2;
     out->kernel = MUSE_KERNEL_TC_12B;
     out->tile_n = bnt;
-    out->chunk = 2;
     out->ctas = sms;
     return MUSE_OK;
   }

@@ -16,7 +16,10 @@
 //
 // W sources: kTwelve = false: the packed BF16 tiles (two 16 KB tiles of 128 rows, copied to one
 // 32 KB B tile); kTwelve = true: the 12-bit blocks of tc12.cuh (two 12416-byte blocks a unit),
-// decoded by eight decoder warps (thread r = row r of the 256) into a 32 KB B tile.
+// decoded in place by eight decoder warps (thread r = row r of the 256): every decoder reads its
+// row and escapes into registers, a named barrier, then the stage is overwritten with the 32 KB
+// BF16 B tile the UMMA reads. So a stage is 32 KB for both sources and no separate decoded ring
+// is needed.
 //
 // Warps: 0 producer (lane 0), 1 TMEM owner + UMMA issuer (lane 0), 2..5 epilogue (TMEM lane
 // quarter = warp % 4), 6..13 decoders (kTwelve only).
@@ -33,12 +36,11 @@ constexpr int kSnAWindow = 16384;  // the 128-row A window the MMA reads from an
 
 __host__ __device__ constexpr int sn_threads(bool twelve) { return twelve ? 448 : 192; }
 __host__ __device__ constexpr int sn_xbytes(int bnt) { return bnt * 128; }
-__host__ __device__ constexpr int sn_wbytes(bool twelve) { return twelve ? 2 * kT12Block : kSnBTile; }
-// Layout: x ring | (12-bit: decoded ring) | W ring | barriers. The ring after the x ring is at
-// least 32 KB, so the last x stage's 16 KB A window stays inside the allocation.
-__host__ __device__ constexpr int sn_smem(bool twelve, int bnt, int stages, int dstages) {
-  return 1024 + stages * sn_xbytes(bnt) + (twelve ? dstages * kSnBTile : 0) + stages * sn_wbytes(twelve) +
-         (4 * stages + 2 * dstages + 4) * 8 + 16;
+// Layout: x ring | W ring (32 KB stages) | escape areas (12-bit: 2 x 128 B a stage) | barriers.
+// The W ring follows the x ring and is at least 64 KB, so the last x stage's 16 KB A window stays
+// inside the allocation.
+__host__ __device__ constexpr int sn_smem(int bnt, int stages) {
+  return 1024 + stages * (sn_xbytes(bnt) + kSnBTile + 256) + (3 * stages + 4) * 8 + 32;
 }
 
 struct SnArgs {
@@ -48,7 +50,7 @@ struct SnArgs {
   uint16_t* y;              // [M, N]
   float* partials;          // [tiles][smax][BNT][256]
   int* counters;            // [tiles], zero between launches
-  int M, N, stages, dstages;
+  int M, N, stages;
   int rtiles, rpairs, nkb, ttiles;
   long long units;
   int smax;
@@ -61,7 +63,7 @@ template <bool kTwelve, int BNT>
 __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
     tc_skinny_kernel(const __grid_constant__ CUtensorMap tmx, const SnArgs a) {
   constexpr int kX = sn_xbytes(BNT);
-  constexpr int kW = sn_wbytes(kTwelve);
+  constexpr int kW = kSnBTile;
   constexpr int kBlk = kTwelve ? kT12Block : 16384;  // one 128-row block of a unit
   constexpr uint32_t kIdesc = umma_idesc_bf16(128, kSnRows);
   constexpr uint32_t kCols = 512;  // two 256-column accumulators
@@ -71,19 +73,18 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
   const unsigned long long t_start = tracing ? globaltimer() : 0ull;
   unsigned long long t_ready = 0ull, t_main = 0ull;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int stages = a.stages, dstages = kTwelve ? a.dstages : 0;
-  uint8_t* sx = smem;                                               // [stages][BNT x 64 BF16]
-  uint8_t* sdec = sx + static_cast<size_t>(stages) * kX;            // [dstages][32 KB] (12-bit)
-  uint8_t* sw = sdec + static_cast<size_t>(dstages) * kSnBTile;     // [stages][kW]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sw + static_cast<size_t>(stages) * kW);
-  uint64_t* empty = full + stages;                 // W slot free: UMMA commit (BF16) or the decoder warps (12-bit)
-  uint64_t* xempty = empty + stages;               // 12-bit: x slot free (UMMA commit)
-  uint64_t* dec_full = xempty + stages;            // [dstages] decoder warps
-  uint64_t* dec_empty = dec_full + dstages;        // [dstages] UMMA commit
-  uint64_t* acc_full = dec_empty + dstages;        // [2]
+  const int stages = a.stages;
+  uint8_t* sx = smem;                                      // [stages][BNT x 64 BF16]
+  uint8_t* sw = sx + static_cast<size_t>(stages) * kX;     // [stages][32 KB], 1024-aligned
+  uint32_t* sesc = reinterpret_cast<uint32_t*>(sw + static_cast<size_t>(stages) * kW);  // [stages][2][32]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sesc + static_cast<size_t>(stages) * 64);
+  uint64_t* empty = full + stages;                 // UMMA commit: the stage may be refilled
+  uint64_t* decoded = empty + stages;              // 12-bit: the decoder warps have written the B tile
+  uint64_t* acc_full = decoded + stages;           // [2]
   uint64_t* acc_empty = acc_full + 2;              // [2] epilogue warps
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* dec_abort = last_flag + 1;  // [2] 12-bit: a decoder group's wait failed; the group stops together
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -97,17 +98,15 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
     prefetch_tensormap(&tmx);
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kTwelve ? kDecWarps : 1);
-      mbar_init(&xempty[s], 1);
-    }
-    for (int d = 0; d < dstages; ++d) {
-      mbar_init(&dec_full[d], kDecWarps);
-      mbar_init(&dec_empty[d], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&decoded[s], kDecWarps > 0 ? kDecWarps / 2 : 1);  // one decoder group a unit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
     }
+    dec_abort[0] = 0;
+    dec_abort[1] = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kCols);
@@ -159,10 +158,7 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
       for (int i = 0; i < n_units; ++i, ring.next(stages), step(p)) {
         const int s = ring.slot;
         if (i >= pre) {
-          // 12-bit: the decoders free the W block as soon as they have read it; the x tile of the
-          // same slot is free once the UMMA that read it has completed.
           if (!mbar_wait(&empty[s], ring.phase ^ 1u, kErrTcProducer)) break;
-          if (kTwelve && !mbar_wait(&xempty[s], ring.phase ^ 1u, kErrTcProducer)) break;
           issue_w(p, s);
         }
         tma_load_2d(sx + static_cast<size_t>(s) * kX, &tmx, &full[s], p.kb * 64, p.tt * BNT, pol_x);
@@ -176,7 +172,7 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
     if (lane == 0) {
       int kb = p0.kb;
       int seg = 0;
-      Ring rs, rd;
+      Ring rs;
       for (int i = 0; i < n_units;) {
         const int b = seg & 1;
         if (!mbar_wait(&acc_empty[b], static_cast<uint32_t>((seg >> 1) & 1) ^ 1u, kErrTcMma)) {
@@ -187,23 +183,18 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
         const uint32_t acc = tmem + static_cast<uint32_t>(b * kSnRows);
         bool ok = true, first = true;
         for (; i < n_units; ++i) {  // one segment: until this output tile's k blocks end
-          if ((kTwelve && !mbar_wait(&dec_full[rd.slot], rd.phase, kErrTcMma)) ||
+          if ((kTwelve && !mbar_wait(&decoded[rs.slot], rs.phase, kErrTcMma)) ||
               !mbar_wait(&full[rs.slot], rs.phase, kErrTcMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint64_t da = umma_desc_sw128(smem_u32(sx + static_cast<size_t>(rs.slot) * kX));
-          const uint64_t db = umma_desc_sw128(
-              smem_u32(kTwelve ? sdec + static_cast<size_t>(rd.slot) * kSnBTile : sw + static_cast<size_t>(rs.slot) * kW));
+          const uint64_t db = umma_desc_sw128(smem_u32(sw + static_cast<size_t>(rs.slot) * kW));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) umma_bf16(acc, da + 2 * kk, db + 2 * kk, kIdesc, (first && kk == 0) ? 0u : 1u);
           first = false;
-          if (kTwelve) {
-            umma_commit(&dec_empty[rd.slot]);
-            rd.next(dstages);
-          }
-          umma_commit(kTwelve ? &xempty[rs.slot] : &empty[rs.slot]);
+          umma_commit(&empty[rs.slot]);
           rs.next(stages);
           if (++kb == nkb) {
             kb = 0;
@@ -218,64 +209,99 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
     }
     pdl_launch_dependents();
   } else if (kTwelve && warp >= 6) {
-    // Decoders: thread r = row r of the unit's 256 rows (block h = r / 128, its row r % 128).
-    const int r = (warp - 6) * 32 + lane;
-    const int h = r >> 7, rb = r & 127, swz = r & 7;
-    Ring rs, rd;
+    // Decoders: two groups of four warps take alternate units (group g: units i with i % 2 == g),
+    // so two units' load / decode / store chains overlap. Thread t of a group decodes row t of
+    // both blocks of its units (rows t and t + 128 of the B tile).
+    const int grp = (warp - 6) >> 2;
+    const int t = ((warp - 6) & 3) * 32 + lane;
+    const int swz = t & 7;  // (t + 128) % 8 == t % 8
+    int* abort_flag = dec_abort + grp;
+    Ring rs;
     Pos p = p0;
-    for (int i = 0; i < n_units; ++i, rs.next(stages), rd.next(dstages), step(p)) {
-      const int s = rs.slot, d = rd.slot;
-      bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], rs.phase, kErrTcEpilogue));
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&dec_empty[d], rd.phase ^ 1u, kErrTcEpilogue));
-      if (!ok) break;
-      const int rt = 2 * p.rp + h;
-      if (rt < a.rtiles) {  // warp-uniform: a warp's rows are in one block
-        const uint8_t* blk = sw + static_cast<size_t>(s) * kW + h * kT12Block;
-        const uint32_t* area = reinterpret_cast<const uint32_t*>(blk + kT12Raw);
-        const uint4 l0 = *reinterpret_cast<const uint4*>(blk + rb * 16);
-        const uint4 l1 = *reinterpret_cast<const uint4*>(blk + 2048 + rb * 16);
-        const uint4 l2 = *reinterpret_cast<const uint4*>(blk + 4096 + rb * 16);
-        const uint4 l3 = *reinterpret_cast<const uint4*>(blk + 6144 + rb * 16);
-        const uint4 c0 = *reinterpret_cast<const uint4*>(blk + 8192 + rb * 16);
-        const uint4 c1 = *reinterpret_cast<const uint4*>(blk + 10240 + rb * 16);
-        const uint32_t head = area[0];
-        const uint32_t base4 = (head >> 16) * 0x01010101u;
-        const uint32_t l03 = base4 + 0x03020100u, l47 = base4 + 0x07060504u;
-        const int n_esc = static_cast<int>(head & 0xFFFFu);
-        uint8_t* drow = sdec + static_cast<size_t>(d) * kSnBTile + r * 128;
-        *reinterpret_cast<uint4*>(drow + ((0 ^ swz) << 4)) = decode12_bf16x8(l0.x, l0.y, c0.x, l03, l47);
-        *reinterpret_cast<uint4*>(drow + ((1 ^ swz) << 4)) = decode12_bf16x8(l0.z, l0.w, c0.y, l03, l47);
-        *reinterpret_cast<uint4*>(drow + ((2 ^ swz) << 4)) = decode12_bf16x8(l1.x, l1.y, c0.z, l03, l47);
-        *reinterpret_cast<uint4*>(drow + ((3 ^ swz) << 4)) = decode12_bf16x8(l1.z, l1.w, c0.w, l03, l47);
-        *reinterpret_cast<uint4*>(drow + ((4 ^ swz) << 4)) = decode12_bf16x8(l2.x, l2.y, c1.x, l03, l47);
-        *reinterpret_cast<uint4*>(drow + ((5 ^ swz) << 4)) = decode12_bf16x8(l2.z, l2.w, c1.y, l03, l47);
-        *reinterpret_cast<uint4*>(drow + ((6 ^ swz) << 4)) = decode12_bf16x8(l3.x, l3.y, c1.z, l03, l47);
-        *reinterpret_cast<uint4*>(drow + ((7 ^ swz) << 4)) = decode12_bf16x8(l3.z, l3.w, c1.w, l03, l47);
-        if (n_esc <= kT12EscSlots) {
-          for (int j = 1; j <= n_esc; ++j) {  // the same word across the warp: broadcast reads
-            const uint32_t e = area[j];
-            if (static_cast<int>(e >> 22) == rb) t12_patch(drow, swz, static_cast<int>((e >> 16) & 63u), e);
-          }
-        } else {
-          const int row = rt * 128 + rb;  // escape-dense block: the row's list
-          if (row < a.N) {
-            const int hi = __ldg(a.esc_ptr + row + 1);
-            for (int e = t12_lower_bound(a.esc_val, __ldg(a.esc_ptr + row), hi, static_cast<uint32_t>(p.kb * 64));
-                 e < hi; ++e) {
-              const uint32_t v = __ldg(a.esc_val + e);
-              const int kk = static_cast<int>(v >> 16) - p.kb * 64;
-              if (kk >= 64) break;
-              t12_patch(drow, swz, kk, v);
+    if (grp == 1 && n_units > 0) {
+      rs.next(stages);
+      step(p);
+    }
+    for (int i = grp; i < n_units; i += 2) {
+      const int s = rs.slot;
+      // Every warp of the group passes the group's named barrier on every unit, also after a
+      // failed wait: a warp whose wait failed raises the group's abort flag before the barrier
+      // and the whole group leaves after it.
+      const bool got = __all_sync(0xffffffffu, mbar_wait(&full[s], rs.phase, kErrTcEpilogue));
+      if (!got && lane == 0) *reinterpret_cast<volatile int*>(abort_flag) = 1;
+      uint8_t* stage = sw + static_cast<size_t>(s) * kW;
+      uint32_t* areas = sesc + static_cast<size_t>(s) * 64;  // this stage's two escape areas
+      const int rt0 = 2 * p.rp;
+      const bool have1 = rt0 + 1 < a.rtiles;  // the unit's second block exists
+      // 1. Read both rows' 64 weights into registers; warp 0 of the group saves the escape
+      //    areas, which the decoded tile overwrites.
+      uint4 w[2][6];
+      uint32_t l03[2] = {0u, 0u}, l47[2] = {0u, 0u};
+      if (got) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (h == 1 && !have1) break;
+          const uint8_t* blk = stage + h * kT12Block;
+#pragma unroll
+          for (int j = 0; j < 6; ++j) w[h][j] = *reinterpret_cast<const uint4*>(blk + j * 2048 + t * 16);
+          const uint32_t* area = reinterpret_cast<const uint32_t*>(blk + kT12Raw);
+          const uint32_t base4 = (area[0] >> 16) * 0x01010101u;
+          l03[h] = base4 + 0x03020100u;
+          l47[h] = base4 + 0x07060504u;
+          if (t < 32) areas[h * 32 + t] = area[t];
+        }
+      }
+      // 2. The group has read its inputs: overwrite the stage with the BF16 B tile.
+      if (grp == 0) asm volatile("bar.sync 2, 128;" ::: "memory");  // warp-uniform branch
+      else asm volatile("bar.sync 3, 128;" ::: "memory");
+      const bool abort = *reinterpret_cast<volatile int*>(abort_flag) != 0;
+      if (got && !abort) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (h == 1 && !have1) break;
+          const int r = h * 128 + t;
+          uint8_t* drow = stage + r * 128;
+          const uint4 l0 = w[h][0], l1 = w[h][1], l2 = w[h][2], l3 = w[h][3], c0 = w[h][4], c1 = w[h][5];
+          // Chunk j (weights 8j .. 8j + 7) goes to 16-byte position j ^ (r % 8) of the row (128-byte swizzle).
+          *reinterpret_cast<uint4*>(drow + ((0 ^ swz) << 4)) = decode12_bf16x8(l0.x, l0.y, c0.x, l03[h], l47[h]);
+          *reinterpret_cast<uint4*>(drow + ((1 ^ swz) << 4)) = decode12_bf16x8(l0.z, l0.w, c0.y, l03[h], l47[h]);
+          *reinterpret_cast<uint4*>(drow + ((2 ^ swz) << 4)) = decode12_bf16x8(l1.x, l1.y, c0.z, l03[h], l47[h]);
+          *reinterpret_cast<uint4*>(drow + ((3 ^ swz) << 4)) = decode12_bf16x8(l1.z, l1.w, c0.w, l03[h], l47[h]);
+          *reinterpret_cast<uint4*>(drow + ((4 ^ swz) << 4)) = decode12_bf16x8(l2.x, l2.y, c1.x, l03[h], l47[h]);
+          *reinterpret_cast<uint4*>(drow + ((5 ^ swz) << 4)) = decode12_bf16x8(l2.z, l2.w, c1.y, l03[h], l47[h]);
+          *reinterpret_cast<uint4*>(drow + ((6 ^ swz) << 4)) = decode12_bf16x8(l3.x, l3.y, c1.z, l03[h], l47[h]);
+          *reinterpret_cast<uint4*>(drow + ((7 ^ swz) << 4)) = decode12_bf16x8(l3.z, l3.w, c1.w, l03[h], l47[h]);
+          const uint32_t* area = areas + h * 32;
+          const int n_esc = static_cast<int>(area[0] & 0xFFFFu);
+          if (n_esc == 0) continue;
+          if (n_esc <= kT12EscSlots) {
+            for (int j = 1; j <= n_esc; ++j) {  // the same word across the warp: broadcast reads
+              const uint32_t e = area[j];
+              if (static_cast<int>(e >> 22) == t) t12_patch(drow, swz, static_cast<int>((e >> 16) & 63u), e);
+            }
+          } else {
+            const int row = (rt0 + h) * 128 + t;  // escape-dense block: the row's list
+            if (row < a.N) {
+              const int hi = __ldg(a.esc_ptr + row + 1);
+              for (int e = t12_lower_bound(a.esc_val, __ldg(a.esc_ptr + row), hi, static_cast<uint32_t>(p.kb * 64));
+                   e < hi; ++e) {
+                const uint32_t v = __ldg(a.esc_val + e);
+                const int kk = static_cast<int>(v >> 16) - p.kb * 64;
+                if (kk >= 64) break;
+                t12_patch(drow, swz, kk, v);
+              }
             }
           }
         }
         fence_proxy_async_smem();  // the tensor cores read this tile through the async proxy
       }
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&dec_full[d]);
-        mbar_arrive(&empty[s]);
-      }
+      if (lane == 0) mbar_arrive(&decoded[s]);
+      if (abort) break;
+      rs.next(stages);
+      rs.next(stages);
+      step(p);
+      step(p);
     }
   } else if (warp >= 2 && warp <= 5) {
     // Epilogue: TMEM lane = token row of the tile, columns = the unit's 256 W rows.
@@ -291,8 +317,8 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
       const bool ok = __all_sync(0xffffffffu, mbar_wait_idle(&acc_full[b], static_cast<uint32_t>((seg >> 1) & 1),
                                                              kErrTcEpilogue));
       tc_fence_after();
+      if (tracing) t_main = globaltimer();  // the last segment's value remains: main loop done
       if (!waited) {
-        if (tracing) t_main = globaltimer();
         pdl_launch_dependents();
         pdl_wait();  // y and the counters may still be in use by the previous grid
         waited = true;

@@ -210,8 +210,8 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], static_cast<uint32_t>((seg >> 1) & 1),
                                                         kErrTcEpilogue));
       tc_fence_after();
+      if (tracing) t_main = globaltimer();  // the last segment's value remains: main loop done
       if (!waited) {
-        if (tracing) t_main = globaltimer();
         pdl_launch_dependents();
         pdl_wait();  // y and the counters may still be in use by the previous grid
         waited = true;

@@ -70,7 +70,7 @@ def test_plan_default_without_device():
     p = _lib.plan_default(1, 10240, 8192, weights_12b=True)
     assert p.kernel == _lib.KERNEL_GEMV_12B
     p = _lib.plan_default(1, 10240, 8192, weights_12b=True, tiles=True)
-    assert p.kernel == _lib.KERNEL_TC_12B and p.tile_n == 16 and p.ctas > 0 and p.chunk == 2
+    assert p.kernel == _lib.KERNEL_TC_12B and p.tile_n == 16 and p.ctas > 0
     p = _lib.plan_default(300, 2304, 8192, weights_12b=True, tiles=True)
     assert p.kernel == _lib.KERNEL_TC_12B and p.tile_n == 128
     with pytest.raises(_lib.MuseError):

@@ -127,7 +127,7 @@ def test_pack_tiles12_layout():
     assert head.max() > 31  # the escape-dense block is covered
 
 
-@pytest.mark.parametrize("n,k,m,tile_n,ctas,stages,dstages", [
+@pytest.mark.parametrize("n,k,m,tile_n,ctas,stages,unused", [
     (200, 1024, 3, 16, 7, 2, 1),
     (2304, 8192, 1, 16, 0, 0, 0),
     (2304, 8192, 16, 16, 148, 5, 2),
@@ -139,13 +139,13 @@ def test_pack_tiles12_layout():
     (6144, 4096, 7, 16, 296, 6, 2),
     (10240, 8192, 1, 16, 148, 4, 3),
 ])
-def test_tc12_parity(n, k, m, tile_n, ctas, stages, dstages):
+def test_tc12_parity(n, k, m, tile_n, ctas, stages, unused):
     wb = _weights(n, k, n + m)
     enc = _Enc12Tiles(wb)
     assert enc.host.n_esc > 0
     xb = bits(torch.randn((m, k), generator=torch.Generator().manual_seed(m)).to(torch.bfloat16))
     x = to_dev(xb)
-    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, tile_n=tile_n, ctas=ctas, stages=stages, chunk=dstages)
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, tile_n=tile_n, ctas=ctas, stages=stages)
     y = _run(enc, x, m, plan)
     yb = bits(y)
     ok, msg, _ = O.check_implementation(xb, wb, yb)
@@ -205,8 +205,8 @@ def test_tc12_errors():
         _lib.proj_12b_tiles(view, enc.tiles.data_ptr(), x.data_ptr(), y.data_ptr(), 4,
                             _lib.MusePlan(kernel=_lib.KERNEL_TC_12B), stream())
     scratch = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
-    for bad in (_lib.MusePlan(kernel=_lib.KERNEL_TC_12B, tile_n=24), _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, chunk=5),
-                _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, stages=40)):
+    for bad in (_lib.MusePlan(kernel=_lib.KERNEL_TC_12B, tile_n=24), _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, tile_n=256),
+                _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, stages=40), _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, stages=1)):
         with pytest.raises(_lib.MuseError):
             _lib.proj_12b_tiles(view, enc.tiles.data_ptr(), x.data_ptr(), y.data_ptr(), 4, bad, stream(),
                                 scratch.data_ptr(), scratch.numel())
