@@ -608,7 +608,7 @@ int sn_shape(bool twelve, int64_t m, int64_t n, int64_t k, const MusePlan& p, Sn
     return fail(MUSE_ERR_PLAN, "%s: tile_n must be 16, 32, 64 or 128 (got %d)", name, bnt);
   const int per_stage = muse::sn_smem(bnt, 1) - muse::sn_smem(bnt, 0);
   const int max_stages = (limit - muse::sn_smem(bnt, 0)) / per_stage;
-  const int stages = p.stages > 0 ? p.stages : std::min(5, max_stages);
+  const int stages = p.stages > 0 ? p.stages : std::min(twelve ? 6 : 5, max_stages);
   if (stages < 2 || stages > max_stages)
     return fail(MUSE_ERR_PLAN, "%s: %d stages do not fit (max %d)", name, stages, max_stages);
   SnShape sh;

@@ -271,16 +271,9 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
           *reinterpret_cast<uint4*>(drow + ((5 ^ swz) << 4)) = decode12_bf16x8(l2.z, l2.w, c1.y, l03[h], l47[h]);
           *reinterpret_cast<uint4*>(drow + ((6 ^ swz) << 4)) = decode12_bf16x8(l3.x, l3.y, c1.z, l03[h], l47[h]);
           *reinterpret_cast<uint4*>(drow + ((7 ^ swz) << 4)) = decode12_bf16x8(l3.z, l3.w, c1.w, l03[h], l47[h]);
-          const uint32_t* area = areas + h * 32;
-          const int n_esc = static_cast<int>(area[0] & 0xFFFFu);
-          if (n_esc == 0) continue;
-          if (n_esc <= kT12EscSlots) {
-            for (int j = 1; j <= n_esc; ++j) {  // the same word across the warp: broadcast reads
-              const uint32_t e = area[j];
-              if (static_cast<int>(e >> 22) == t) t12_patch(drow, swz, static_cast<int>((e >> 16) & 63u), e);
-            }
-          } else {
-            const int row = (rt0 + h) * 128 + t;  // escape-dense block: the row's list
+          const int n_esc = static_cast<int>(areas[h * 32] & 0xFFFFu);
+          if (n_esc > kT12EscSlots) {
+            const int row = (rt0 + h) * 128 + t;  // escape-dense block: each row owner walks its list
             if (row < a.N) {
               const int hi = __ldg(a.esc_ptr + row + 1);
               for (int e = t12_lower_bound(a.esc_val, __ldg(a.esc_ptr + row), hi, static_cast<uint32_t>(p.kb * 64));
@@ -290,6 +283,24 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
                 if (kk >= 64) break;
                 t12_patch(drow, swz, kk, v);
               }
+            }
+          }
+        }
+        // 3. Escapes listed in the areas: once every row is written (group barrier), thread j of the
+        //    group writes entry j's exact bits. The escape counts are the same for the whole group.
+        const int ne0 = static_cast<int>(areas[0] & 0xFFFFu);
+        const int ne1 = have1 ? static_cast<int>(areas[32] & 0xFFFFu) : 0;
+        const bool listed0 = ne0 > 0 && ne0 <= kT12EscSlots, listed1 = ne1 > 0 && ne1 <= kT12EscSlots;
+        if (listed0 || listed1) {
+          if (grp == 0) asm volatile("bar.sync 2, 128;" ::: "memory");  // warp-uniform branch
+          else asm volatile("bar.sync 3, 128;" ::: "memory");
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int ne = h == 0 ? (listed0 ? ne0 : 0) : (listed1 ? ne1 : 0);
+            if (t < ne) {
+              const uint32_t e = areas[h * 32 + 1 + t];
+              const int row = h * 128 + static_cast<int>(e >> 22);
+              t12_patch(stage + row * 128, row & 7, static_cast<int>((e >> 16) & 63u), e);
             }
           }
         }
