@@ -39,6 +39,7 @@ extern "C" {
 #define MUSE_KERNEL_TC_GEMM2 6   /* persistent tcgen05 GEMM on CTA pairs (cta_group::2), 256 x 256 a tile */
 #define MUSE_KERNEL_TC_12B 7     /* stream-K tcgen05 on 12-bit tiles: W decoded to BF16 in shared memory */
 #define MUSE_KERNEL_TC_SKINNY 8  /* stream-K tcgen05 over packed tiles with W as the B operand (256 W rows an MMA) */
+#define MUSE_KERNEL_F32_GEMV 9   /* FP32 W on CUDA cores (the router), M <= 8 */
 
 /* Plan flags. */
 #define MUSE_FLAG_GLOBAL_SPLIT 1 /* TC_TILE: reduce K-split partials through caller scratch instead of a cluster */
@@ -98,6 +99,7 @@ int muse_device_error(int* code, void* stream);
 #define MUSE_WEIGHTS_12B 1       /* 12-bit planes (muse_proj_12b) */
 #define MUSE_WEIGHTS_TILES 2     /* packed tiles (muse_proj_bf16_tiles; TC_GEMM2 and TC_STREAMK plans need scratch) */
 #define MUSE_WEIGHTS_12B_TILES 3 /* 12-bit tiles (muse_proj_12b_tiles; needs scratch) */
+#define MUSE_WEIGHTS_F32 4        /* FP32 W and its hi | lo tiles (muse_proj_f32, the router) */
 
 /*
  * The library's default plan for a shape and weight format (MUSE_WEIGHTS_*). Replaces the
@@ -210,6 +212,31 @@ int muse_pack_tiles12(const MuseEnc12* enc, void* tiles12, void* stream);
  */
 int muse_proj_12b_tiles(const MuseEnc12* enc, const void* tiles12, const void* x, void* y, int64_t m,
                         const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream);
+
+/* Device bytes of the router tiles muse_pack_router writes for an FP32 W [N, K]: the packed tiles
+ * (muse_pack_tiles layout) of the BF16 matrix [hi | lo] of N rows and 2K columns. */
+int muse_router_tiles_bytes(int64_t n, int64_t k, int64_t* bytes);
+
+/*
+ * Packs an FP32 W [N, K] (device, K % 64 == 0) as the tiles of [hi | lo]: hi = BF16(W) and
+ * lo = BF16(W - hi), both rounded to nearest even. Replaces the router_hi / router_lo split of the
+ * reference's prepare (submission.py:1120-1124). Device kernel on `stream`.
+ */
+int muse_pack_router(const float* w, void* tiles, int64_t n, int64_t k, void* stream);
+
+/*
+ * y = x . W^T for an FP32 W [N, K] (the router): x BF16 [M, K], y FP32 [M, N]. plan->kernel:
+ *   MUSE_KERNEL_F32_GEMV: W read in FP32 on CUDA cores, FP32 accumulation, M <= 8 (`tiles` unused);
+ *     replaces router_fp32 / _router_fp32_kernel (submission.py:1027-1042, 131-169);
+ *   MUSE_KERNEL_TC_TILE: x . hi^T + x . lo^T as one K = 2K tensor-core projection over the tiles of
+ *     muse_pack_router, FP32 accumulation and output (`w` unused); split-K plans take scratch as in
+ *     muse_proj_bf16_tiles (muse_scratch_bytes with the same M, N, K); replaces router_hilo /
+ *     _router_hilo_tma_kernel (submission.py:1053-1075, 172-207), which added its K splits into a
+ *     zeroed output with atomics: here the last split sums them in rank order (deterministic).
+ * K % 64 == 0; x 16-byte aligned.
+ */
+int muse_proj_f32(const void* x, const float* w, const void* tiles, float* y, int64_t m, int64_t n, int64_t k,
+                  const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream);
 
 /* Host buffer sizes for muse_encode12: planes and bases bytes. */
 int muse_encode12_sizes(int64_t n, int64_t k, int64_t* planes_bytes, int64_t* bases_bytes);

@@ -17,10 +17,10 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 MUSE_OK = 0
 ERRORS = {-1: "INVALID", -2: "ALIGN", -3: "SHAPE", -4: "CAPACITY", -5: "CUDA", -6: "TIMEOUT", -7: "PLAN"}
 KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_GEMM, KERNEL_TC_GEMM2 = 1, 2, 3, 4, 5, 6
-KERNEL_TC_12B, KERNEL_TC_SKINNY = 7, 8
+KERNEL_TC_12B, KERNEL_TC_SKINNY, KERNEL_F32_GEMV = 7, 8, 9
 KERNEL_NAMES = {KERNEL_GEMV_BF16: "gemv_bf16", KERNEL_GEMV_12B: "gemv_12b", KERNEL_TC_TILE: "tc_tile",
                 KERNEL_TC_STREAMK: "tc_streamk", KERNEL_TC_GEMM: "tc_gemm", KERNEL_TC_GEMM2: "tc_gemm2",
-                KERNEL_TC_12B: "tc_12b", KERNEL_TC_SKINNY: "tc_skinny"}
+                KERNEL_TC_12B: "tc_12b", KERNEL_TC_SKINNY: "tc_skinny", KERNEL_F32_GEMV: "f32_gemv"}
 TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_SKINNY, KERNEL_TC_GEMM, KERNEL_TC_GEMM2)
 KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
 FLAG_GLOBAL_SPLIT = 1
@@ -80,6 +80,9 @@ _SIGNATURES = {
     "muse_tiles12_bytes": ([_I64, _I64, ctypes.POINTER(_I64)], _I32),
     "muse_pack_tiles12": ([ctypes.POINTER(MuseEnc12), _P, _P], _I32),
     "muse_proj_12b_tiles": ([ctypes.POINTER(MuseEnc12), _P, _P, _P, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
+    "muse_router_tiles_bytes": ([_I64, _I64, ctypes.POINTER(_I64)], _I32),
+    "muse_pack_router": ([_P, _P, _I64, _I64, _P], _I32),
+    "muse_proj_f32": ([_P, _P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
     "muse_proj_bf16_tiles_noalloc": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P], _I32),
     "muse_encode12_sizes": ([_I64, _I64, ctypes.POINTER(_I64), ctypes.POINTER(_I64)], _I32),
     "muse_encode12": ([_P, _I64, _I64, _P, _P, _P, _P, _I64, ctypes.POINTER(_I64), _I32], _I32),
@@ -134,13 +137,16 @@ def device_error(stream: int = 0) -> int:
     return code.value
 
 
-WEIGHTS_ROW_MAJOR, WEIGHTS_12B, WEIGHTS_TILES, WEIGHTS_12B_TILES = 0, 1, 2, 3
+WEIGHTS_ROW_MAJOR, WEIGHTS_12B, WEIGHTS_TILES, WEIGHTS_12B_TILES, WEIGHTS_F32 = 0, 1, 2, 3, 4
 
 
-def plan_default(m: int, n: int, k: int, weights_12b: bool = False, tiles: bool = False) -> MusePlan:
-    """The library's default plan; weights_12b with tiles means the 12-bit tiles (TC_12B)."""
+def plan_default(m: int, n: int, k: int, weights_12b: bool = False, tiles: bool = False, f32: bool = False) -> MusePlan:
+    """The library's default plan; weights_12b with tiles means the 12-bit tiles (TC_12B); f32: the
+    router's FP32 W with its hi | lo tiles."""
     p = MusePlan()
-    if weights_12b:
+    if f32:
+        fmt = WEIGHTS_F32
+    elif weights_12b:
         fmt = WEIGHTS_12B_TILES if tiles else WEIGHTS_12B
     else:
         fmt = WEIGHTS_TILES if tiles else WEIGHTS_ROW_MAJOR
@@ -194,6 +200,22 @@ def proj_12b_tiles(enc: MuseEnc12, tiles12_ptr: int, x_ptr: int, y_ptr: int, m: 
                    scratch_ptr: int = 0, scratch_bytes: int = 0) -> None:
     check(load().muse_proj_12b_tiles(ctypes.byref(enc), tiles12_ptr, x_ptr, y_ptr, m, ctypes.byref(plan),
                                      scratch_ptr or None, scratch_bytes, ctypes.c_void_p(stream)))
+
+
+def router_tiles_bytes(n: int, k: int) -> int:
+    out = ctypes.c_int64()
+    check(load().muse_router_tiles_bytes(n, k, ctypes.byref(out)))
+    return out.value
+
+
+def pack_router(w_ptr: int, tiles_ptr: int, n: int, k: int, stream: int) -> None:
+    check(load().muse_pack_router(w_ptr, tiles_ptr, n, k, ctypes.c_void_p(stream)))
+
+
+def proj_f32(x_ptr: int, w_ptr: int, tiles_ptr: int, y_ptr: int, m: int, n: int, k: int, plan: MusePlan, stream: int,
+             scratch_ptr: int = 0, scratch_bytes: int = 0) -> None:
+    check(load().muse_proj_f32(x_ptr, w_ptr or None, tiles_ptr or None, y_ptr, m, n, k, ctypes.byref(plan),
+                               scratch_ptr or None, scratch_bytes, ctypes.c_void_p(stream)))
 
 
 TRACE_RECORD_BYTES = 48

@@ -20,6 +20,7 @@
 #include "tc_gemm2.cuh"
 #include "tc12.cuh"
 #include "tc_skinny.cuh"
+#include "router.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -297,8 +298,10 @@ int launch_tc_t(const CUtensorMap& tmw, const CUtensorMap& tmx, const muse::TcAr
 }
 
 // W is row-major (tiles == nullptr) or packed tiles (w == nullptr).
+// y32 != nullptr: FP32 output; kx > 0: x has kx columns and W (tiles) 2 * kx (the router's hi | lo).
 int run_tc_tile(const void* x, const void* w, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
-                const MusePlan& p, void* scratch, int64_t scratch_bytes, cudaStream_t st) {
+                const MusePlan& p, void* scratch, int64_t scratch_bytes, cudaStream_t st, float* y32 = nullptr,
+                int64_t kx = 0) {
   TcShape sh;
   if (int rc = tc_shape(m, n, k, p, &sh)) return rc;
   const int64_t need = tc_scratch_bytes(sh);
@@ -312,10 +315,12 @@ int run_tc_tile(const void* x, const void* w, const void* tiles, void* y, int64_
   if (!tiles) {
     if (int rc = make_map(&tmw, w, n, k, 128)) return rc;
   }
-  if (int rc = make_map(&tmx, x, m, k, sh.bnt)) return rc;
+  if (int rc = make_map(&tmx, x, m, kx > 0 ? kx : k, sh.bnt)) return rc;
   muse::TcArgs a;
   a.wtiles = static_cast<const uint8_t*>(tiles);
   a.y = static_cast<uint16_t*>(y);
+  a.y32 = y32;
+  a.kxb = kx > 0 ? static_cast<int>(kx / muse::kTcBK) : 0;
   a.counters = need > 0 ? static_cast<int*>(scratch) : nullptr;
   a.partials = need > 0 ? reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kCounterBytes) : nullptr;
   a.M = static_cast<int>(m);
@@ -751,8 +756,8 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
   muse::clear_error();
   if (!out) return fail(MUSE_ERR_INVALID, "plan_default: null output");
   if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "plan_default: non-positive size");
-  if (weights < MUSE_WEIGHTS_ROW_MAJOR || weights > MUSE_WEIGHTS_12B_TILES)
-    return fail(MUSE_ERR_INVALID, "plan_default: weights must be MUSE_WEIGHTS_ROW_MAJOR, _12B, _TILES or _12B_TILES");
+  if (weights < MUSE_WEIGHTS_ROW_MAJOR || weights > MUSE_WEIGHTS_F32)
+    return fail(MUSE_ERR_INVALID, "plan_default: weights must be one of MUSE_WEIGHTS_*");
   DeviceInfo* d;
   int sms = 148;
   if (device_info(&d) == MUSE_OK) sms = d->sms;
@@ -762,6 +767,24 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
     out->kernel = MUSE_KERNEL_GEMV_12B;
     out->warps = 16;
     return m <= 8 ? MUSE_OK : fail(MUSE_ERR_SHAPE, "plan_default: 12-bit weights serve M <= 8");
+  }
+  if (weights == MUSE_WEIGHTS_F32) {
+    // The router: FP32 on CUDA cores up to 8 tokens, BF16 hi + lo tiles (K = 2k) above.
+    if (m <= 8) {
+      out->kernel = MUSE_KERNEL_F32_GEMV;
+      return MUSE_OK;
+    }
+    int bnt = 16;
+    while (bnt < m && bnt < 256) bnt *= 2;
+    out->kernel = MUSE_KERNEL_TC_TILE;
+    out->tile_n = bnt;
+    const int64_t tiles = ((n + 127) / 128) * ((m + bnt - 1) / bnt);
+    int64_t split = tiles >= sms ? 1 : sms / tiles;
+    split = std::max<int64_t>(1, std::min<int64_t>({split, 32, (2 * k) / 64}));
+    out->split = static_cast<int>(split);
+    out->stages = bnt <= 64 ? 6 : 0;
+    if (split > 1) out->flags = MUSE_FLAG_GLOBAL_SPLIT;
+    return MUSE_OK;
   }
   if (weights == MUSE_WEIGHTS_12B_TILES) {
     // Stream-K over the 12-bit blocks: one CTA an SM with a deep ring.
@@ -966,6 +989,61 @@ int muse_proj_12b_tiles(const MuseEnc12* enc, const void* tiles12, const void* x
   if (plan->kernel != MUSE_KERNEL_TC_12B) return fail(MUSE_ERR_PLAN, "proj_12b_tiles: plan kernel must be TC_12B");
   return run_skinny(true, tiles12, enc, x, y, m, enc->n, enc->k, *plan, scratch, scratch_bytes,
                     static_cast<cudaStream_t>(stream));
+}
+
+int muse_router_tiles_bytes(int64_t n, int64_t k, int64_t* bytes) {
+  muse::clear_error();
+  if (!bytes) return fail(MUSE_ERR_INVALID, "router_tiles_bytes: null output");
+  if (n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "router_tiles_bytes: non-positive size");
+  if (k % 64) return fail(MUSE_ERR_SHAPE, "router_tiles_bytes: K must be a multiple of 64");
+  *bytes = ((n + 127) / 128) * ((2 * k) / 64) * int64_t(muse::kTcABytes);
+  return MUSE_OK;
+}
+
+int muse_pack_router(const float* w, void* tiles, int64_t n, int64_t k, void* stream) {
+  muse::clear_error();
+  if (!w || !tiles) return fail(MUSE_ERR_INVALID, "pack_router: null pointer");
+  if (n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "pack_router: non-positive size");
+  if (k % 64) return fail(MUSE_ERR_SHAPE, "pack_router: K must be a multiple of 64");
+  if (!aligned16(w) || !aligned16(tiles)) return fail(MUSE_ERR_ALIGN, "pack_router: 16-byte alignment needed");
+  if (n > (int64_t(1) << 24) || k > (int64_t(1) << 23)) return fail(MUSE_ERR_SHAPE, "pack_router: dimension too large");
+  const int nkb = static_cast<int>((2 * k) / 64);
+  const long long chunks = ((n + 127) / 128) * static_cast<long long>(nkb) * 1024;
+  const int blocks = static_cast<int>(std::min<long long>((chunks + 255) / 256, 148 * 32));
+  muse::pack_router_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      w, static_cast<uint4*>(tiles), static_cast<int>(n), static_cast<int>(k), nkb, chunks);
+  return launch_error("pack_router launch");
+}
+
+int muse_proj_f32(const void* x, const float* w, const void* tiles, float* y, int64_t m, int64_t n, int64_t k,
+                  const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream) {
+  muse::clear_error();
+  if (!x || !y || !plan) return fail(MUSE_ERR_INVALID, "proj_f32: null pointer");
+  if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "proj_f32: non-positive size");
+  if (k % 64) return fail(MUSE_ERR_SHAPE, "proj_f32: K must be a multiple of 64");
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(y) & 3u))
+    return fail(MUSE_ERR_ALIGN, "proj_f32: x 16-byte aligned, y 4-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (plan->kernel == MUSE_KERNEL_F32_GEMV) {
+    if (!w) return fail(MUSE_ERR_INVALID, "proj_f32: the FP32 kernel reads W: null pointer");
+    if (!aligned16(w)) return fail(MUSE_ERR_ALIGN, "proj_f32: W must be 16-byte aligned");
+    if (m > 8) return fail(MUSE_ERR_SHAPE, "proj_f32: the FP32 kernel serves M <= 8 (got %lld)", (long long)m);
+    if (n > 0x7FFFFFFF) return fail(MUSE_ERR_SHAPE, "proj_f32: N too large");
+    const float* wf = w;
+    const uint16_t* xb = static_cast<const uint16_t*>(x);
+    const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
+    const dim3 grid(static_cast<unsigned>(n));
+    if (m <= 1) muse::router_f32_kernel<1><<<grid, muse::kRouterThreads, 0, st>>>(wf, xb, y, mi, ni, ki);
+    else if (m <= 2) muse::router_f32_kernel<2><<<grid, muse::kRouterThreads, 0, st>>>(wf, xb, y, mi, ni, ki);
+    else if (m <= 4) muse::router_f32_kernel<4><<<grid, muse::kRouterThreads, 0, st>>>(wf, xb, y, mi, ni, ki);
+    else muse::router_f32_kernel<8><<<grid, muse::kRouterThreads, 0, st>>>(wf, xb, y, mi, ni, ki);
+    return launch_error("router_f32 launch");
+  }
+  if (plan->kernel != MUSE_KERNEL_TC_TILE)
+    return fail(MUSE_ERR_PLAN, "proj_f32: plan kernel must be F32_GEMV or TC_TILE");
+  if (!tiles) return fail(MUSE_ERR_INVALID, "proj_f32: the tensor-core path reads the hi | lo tiles: null pointer");
+  if (!aligned16(tiles)) return fail(MUSE_ERR_ALIGN, "proj_f32: tiles must be 16-byte aligned");
+  return run_tc_tile(x, nullptr, tiles, nullptr, m, n, 2 * k, *plan, scratch, scratch_bytes, st, y, k);
 }
 
 }  // extern "C"

@@ -43,7 +43,9 @@ __host__ __device__ constexpr int tc_tile_smem(int bnt, int stages) {
 
 struct TcArgs {
   const uint8_t* wtiles;  // packed tiles (mode & kTcModeTiles)
-  uint16_t* y;            // [M, N]
+  uint16_t* y;            // [M, N] BF16, or
+  float* y32;             // [M, N] FP32 when not null (the router)
+  int kxb;                // x's K in 64-blocks when W's K is twice x's (router hi | lo), else 0
   float* partials;        // global split: [tiles][split][BNT][128]
   int* counters;          // global split: [tiles], zero between launches
   int M, N, K, split, stages, mode;
@@ -93,6 +95,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   float* part = reinterpret_cast<float*>(smem);  // [BNT][128], reuses the ring after the main loop
 
   const bool tiles_mode = (a.mode & kTcModeTiles) != 0;
+  auto store = [&](int m, int n, float v) {  // y[m, n] in the output's precision
+    if (a.y32 != nullptr) a.y32[static_cast<size_t>(m) * a.N + n] = v;
+    else a.y[static_cast<size_t>(m) * a.N + n] = f32_to_bf16(v);
+  };
   const bool global_split = (a.mode & kTcModeGlobalSplit) != 0;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -140,9 +146,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_expect_tx(&full[i], static_cast<uint32_t>(kTcABytes + kBBytes));
         load_w(i, i);
       }
+      // x's K block for W's K block kb: the same, or kb - kxb past x's end (W = [hi | lo]).
+      auto xcol = [&](int kb) { return (a.kxb > 0 && kb >= a.kxb ? kb - a.kxb : kb) * kTcBK; };
       pdl_wait();
       for (int i = 0; i < pre; ++i)
-        tma_load_2d(sb + static_cast<size_t>(i) * kBBytes, &tmx, &full[i], (kb0 + i) * kTcBK, tt * BNT, pol_x);
+        tma_load_2d(sb + static_cast<size_t>(i) * kBBytes, &tmx, &full[i], xcol(kb0 + i), tt * BNT, pol_x);
       int issued = pre;
       Ring ring;  // position of unit pre
       for (int i = 0; i < pre; ++i) ring.next(stages);
@@ -151,7 +159,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!mbar_wait(&empty[s], ring.phase ^ 1u, kErrTcProducer)) break;
         mbar_expect_tx(&full[s], static_cast<uint32_t>(kTcABytes + kBBytes));
         load_w(i, s);
-        tma_load_2d(sb + static_cast<size_t>(s) * kBBytes, &tmx, &full[s], (kb0 + i) * kTcBK, tt * BNT, pol_x);
+        tma_load_2d(sb + static_cast<size_t>(s) * kBBytes, &tmx, &full[s], xcol(kb0 + i), tt * BNT, pol_x);
         ++issued;
       }
       for (int i = max(0, issued - stages); i < issued; ++i)
@@ -196,7 +204,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = tt * BNT + c + j;
-            if (m < a.M && n < a.N) a.y[static_cast<size_t>(m) * a.N + n] = f32_to_bf16(v[j]);
+            if (m < a.M && n < a.N) store(m, n, v[j]);
           }
         } else if (global_split) {
 #pragma unroll
@@ -222,7 +230,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int m = tt * BNT + c + j;
-              if (m < a.M) a.y[static_cast<size_t>(m) * a.N + n] = f32_to_bf16(sum[j]);
+              if (m < a.M) store(m, n, sum[j]);
             }
           }
         }
@@ -259,7 +267,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int q = 0; q < 8; ++q) {
             const int j = j0 + q * split;
             const int m = tt * BNT + j;
-            if (j < BNT && m < a.M) a.y[static_cast<size_t>(m) * a.N + n] = f32_to_bf16(sum[q]);
+            if (j < BNT && m < a.M) store(m, n, sum[q]);
           }
         }
       }

@@ -1,26 +1,27 @@
-"""The drop-in entry point for the BF16 dense projections: ``prepare(weights)`` once, untimed, then
+"""The drop-in entry point for the dense projections: ``prepare(weights)`` once, untimed, then
 ``kernel_fn(data, state)`` per call (the reference's interface, submission.py:23-41, 1115-1173).
 
 What serves each shape (``kernel_fn`` -> ``project``), chosen per (N, K, M) by the committed sweep
-table (``dispatch.py``), else by the library's default plan:
+table (``dispatch.py``), else by the library's default plan (muse_plan_default):
 
-- few tokens, BF16 W: the streaming CUDA-core GEMV (bulk-copy shared-memory ring, deterministic
-  split-K inside the CTA);
-- few tokens, 12-bit W: the same GEMV reading the lossless 12-bit planes (about 12 bits a weight);
-- more tokens: the tcgen05/TMEM tile kernel, with K split across a thread-block cluster and
-  reduced over DSMEM in a fixed order for skinny shapes.
+- BF16 W, few tokens: the tcgen05 tile kernel on packed W tiles with K split across CTAs (partials
+  reduced in rank order by the last CTA), stream-K variants (W as the UMMA's A or B operand) for
+  large N, and a streaming CUDA-core GEMV where it wins;
+- BF16 W, prefill: persistent tcgen05 GEMMs (CTA pairs with cta_group::2 past M = 256);
+- 12-bit W (opt-in or table rows): lossless 12-bit blocks decoded to BF16 in shared memory and fed
+  to the tensor cores, or the CUDA-core 12-bit GEMV;
+- the FP32 router: W in FP32 on CUDA cores up to 8 tokens, else its BF16 hi + lo pair as one
+  K = 2K tensor-core projection with FP32 accumulation and output (submission.py:1027-1076).
 
-All three are this build's own sm_100a kernels behind the C ABI in include/muse_proj.h. There is
-no cuBLAS, Triton or CPU fallback: a shape the kernels cannot run raises.
+All are this build's own sm_100a kernels behind the C ABI in include/muse_proj.h. There is no
+cuBLAS, Triton or CPU fallback: a shape the kernels cannot run raises.
 
-``prepare`` keeps every BF16 weight resident, builds 12-bit copies of the layers the table serves
-from 12 bits (host encoder, checked lossless bit for bit), and runs a known-answer self-check of
-every planned kernel: one-hot power-of-two rows of x must return exact columns of W (the
-reference's probe-row idea, reference.py:30-35), so a wrong kernel raises in prepare instead of
-serving (the reference instead fell back to Triton/cuBLAS, submission.py:1142-1151).
-
-The FP32 router (reference submission.py:130-205, 1027-1076) is outside this build's BF16 path:
-``kernel_fn`` raises NotImplementedError for it.
+``prepare`` keeps every weight resident, packs the tile copies the tensor-core kernels stream
+(the router's as hi | lo), builds 12-bit copies of the layers the table serves from 12 bits (host
+encoder, checked lossless bit for bit), and runs a known-answer self-check of every planned kernel:
+one-hot power-of-two rows of x must return exact columns of W (the reference's probe-row idea,
+reference.py:30-35; within 1e-5 for the router's hi + lo), so a wrong kernel raises in prepare
+instead of serving (the reference instead fell back to Triton/cuBLAS, submission.py:1142-1151).
 """
 
 from __future__ import annotations
@@ -44,7 +45,7 @@ class Weights(TypedDict):
     o: torch.Tensor         # bfloat16 [8192, 1024]
     pooler: torch.Tensor    # bfloat16 [4096, 8192]
     unpooler: torch.Tensor  # bfloat16 [8192, 4096]; up to 8 tokens, only rows 0-1023 (this GPU's slice)
-    router: torch.Tensor    # float32 [256, 8192] (not served by this build)
+    router: torch.Tensor    # float32 [256, 8192]; FP32 output
 
 
 class Config(TypedDict):
@@ -55,7 +56,7 @@ class Config(TypedDict):
 
 
 class Inputs(TypedDict):
-    x: torch.Tensor  # bfloat16 [M, K]
+    x: torch.Tensor  # bfloat16 [M, K] (the router's too: its weights and output are FP32)
     config: Config
 
 
@@ -100,12 +101,22 @@ def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | 
     12-bit copies; None lets the dispatch table decide."""
     _lib.load()
     disp = dispatch if dispatch is not None else Dispatch()
-    state = {"weights": {}, "tiles": {}, "fp32": {}, "enc12": {}, "dispatch": disp, "checked": [],
+    state = {"weights": {}, "tiles": {}, "fp32": {}, "fp32_tiles": {}, "enc12": {}, "dispatch": disp, "checked": [],
              "scratch": None, "scratch_need": {}, "pdl": pdl, "pdl_plans": {}}
     for name, w in weights.items():
-        if w.dtype != torch.bfloat16:
-            state["fp32"][name] = w.contiguous()
+        if w.dtype == torch.float32:
+            if w.dim() != 2 or not w.is_cuda:
+                raise ValueError(f"{name}: expected a 2-D CUDA tensor, got {tuple(w.shape)} on {w.device}")
+            w = w.contiguous()
+            state["fp32"][name] = w
+            n, k = w.shape
+            # The BF16 hi + lo pair (hi = BF16(W), lo = BF16(W - hi)) as the tiles of [hi | lo].
+            tiles = torch.empty(_lib.router_tiles_bytes(n, k), dtype=torch.uint8, device=w.device)
+            _lib.pack_router(w.data_ptr(), tiles.data_ptr(), n, k, torch.cuda.current_stream(w.device).cuda_stream)
+            state["fp32_tiles"][name] = tiles
             continue
+        if w.dtype != torch.bfloat16:
+            raise ValueError(f"{name}: weights must be bfloat16 or float32, got {w.dtype}")
         if w.dim() != 2 or not w.is_cuda:
             raise ValueError(f"{name}: expected a 2-D CUDA tensor, got {tuple(w.shape)} on {w.device}")
         w = w.contiguous()
@@ -135,6 +146,10 @@ def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | 
                 for m in ms:
                     _known_answer_check(state, name, nn, m)
                     state["checked"].append((name, nn, m))
+        for name, w in state["fp32"].items():
+            for m in (1, 8, 9, 16):  # both FP32 plans: CUDA cores up to 8 tokens, hi + lo above
+                _known_answer_check_f32(state, name, m)
+                state["checked"].append((name, w.shape[0], m))
     torch.cuda.synchronize()
     return state
 
@@ -178,13 +193,70 @@ def _known_answer_check(state: dict, layer: str, n: int, m: int) -> None:
                            f"err {err:.3e}, device error {code:#x}")
 
 
+def _known_answer_check_f32(state: dict, layer: str, m: int) -> None:
+    """The router's one-hot check: row i of y must be 2^p * W[:, c_i] (exact on the FP32 kernel,
+    within 1e-5 relative on hi + lo, whose rounding is ~2^-17 of each weight)."""
+    w = state["fp32"][layer]
+    n, k = w.shape
+    dev = w.device
+    cols = (torch.arange(m, device=dev) * 7919 + 17) % k
+    powers = 2.0 ** (torch.arange(m, device=dev) % 5)
+    x = torch.zeros((m, k), dtype=torch.float32, device=dev)
+    x[torch.arange(m, device=dev), cols] = powers
+    y = project_f32(x.to(torch.bfloat16), state, layer)
+    expect = w[:, cols].T * powers[:, None]
+    plan = _plan_f32(state, m, n, k)
+    if plan.kernel == _lib.KERNEL_F32_GEMV:
+        ok, err = torch.equal(y, expect), (y - expect).abs().max().item()
+    else:
+        err = ((y - expect).norm(dim=1) / expect.norm(dim=1).clamp(min=1e-30)).max().item()
+        ok = err <= 1e-5
+    code = _lib.device_error(torch.cuda.current_stream(dev).cuda_stream)
+    if not ok or code:
+        raise RuntimeError(f"muse self-check failed: {layer} m={m} plan={plan.as_dict()}: err {err:.3e}, "
+                           f"device error {code:#x}")
+
+
+def _plan_f32(state: dict, m: int, n: int, k: int) -> _lib.MusePlan:
+    key = ("f32", m, n, k)
+    plan = state["pdl_plans"].get(key)
+    if plan is None:
+        plan = _lib.plan_default(m, n, k, f32=True)
+        if state.get("pdl", True):
+            plan = _lib.MusePlan.from_dict({**plan.as_dict(), "flags": plan.flags | _lib.FLAG_PDL})
+        state["pdl_plans"][key] = plan
+    return plan
+
+
+def project_f32(x: torch.Tensor, state: dict, layer: str, n: int | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ W[:n].T for an FP32 W (the router): FP32 [m, n]."""
+    w = state["fp32"][layer]
+    big_n, k = w.shape
+    n = big_n if n is None else n
+    if x.dim() != 2 or x.shape[1] != k or x.dtype != torch.bfloat16 or not (0 < n <= big_n):
+        raise ValueError(f"{layer}: x {tuple(x.shape)} {x.dtype}, n={n} does not match W {tuple(w.shape)}")
+    if not x.is_contiguous():
+        x = x.contiguous()
+    if x.data_ptr() % 16:
+        x = x.clone()
+    m = x.shape[0]
+    plan = _plan_f32(state, m, n, k)
+    y = out if out is not None else torch.empty((m, n), dtype=torch.float32, device=x.device)
+    scratch = _scratch_for(state, m, n, k, plan)
+    _lib.proj_f32(x.data_ptr(), w.data_ptr(), state["fp32_tiles"][layer].data_ptr(), y.data_ptr(), m, n, k, plan,
+                  torch.cuda.current_stream(x.device).cuda_stream, scratch.data_ptr() if scratch is not None else 0,
+                  scratch.numel() if scratch is not None else 0)
+    return y
+
+
 def project(x: torch.Tensor, state: dict, layer: str, n: int | None = None,
             out: torch.Tensor | None = None) -> torch.Tensor:
-    """y = x @ W[:n].T (BF16 [m, n]) on this build's kernels."""
+    """y = x @ W[:n].T on this build's kernels: BF16 [m, n], FP32 for an FP32 W (the router)."""
+    if layer in state["fp32"]:
+        return project_f32(x, state, layer, n, out)
     w = state["weights"].get(layer)
     if w is None:
-        if layer in state["fp32"]:
-            raise NotImplementedError(f"{layer}: FP32 weights are outside this build's BF16 projection path")
         raise KeyError(layer)
     big_n, k = w.shape
     n = big_n if n is None else n
@@ -242,6 +314,6 @@ def _scratch_for(state: dict, m: int, n: int, k: int, plan) -> torch.Tensor | No
 
 
 def kernel_fn(data: Inputs, state) -> torch.Tensor:
-    """data["x"] [m, k] BF16 @ W[:n].T -> [m, n] BF16, for data["config"]["layer"]."""
+    """data["x"] [m, k] BF16 @ W[:n].T -> [m, n] BF16 (FP32 for the router), for data["config"]["layer"]."""
     cfg = data["config"]
     return project(data["x"], state, cfg["layer"], cfg["n"])

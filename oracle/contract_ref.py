@@ -113,3 +113,45 @@ def check_implementation(x_bits: np.ndarray, w_bits: np.ndarray, out_bits: np.nd
     if diff[worst] > PROBE_TOL:
         return False, (f"{msg}, but probe row {int(rows[worst])} is off by {diff[worst]:.2e} > {PROBE_TOL:g}"), stats
     return True, f"{msg}; {len(rows)} probe rows exact to {float(diff.max()):.1e}", stats
+
+
+# ---- the FP32 router layer -------------------------------------------------------------------
+
+
+def ref_kernel_f32(x_bits: np.ndarray, w_f32: np.ndarray, n: int | None = None) -> np.ndarray:
+    """reference.py:72-76 for the router: x @ W[:n].T in FP64, rounded to FP32."""
+    x = bf16_to_f32(x_bits).astype(np.float64)
+    w = np.asarray(w_f32 if n is None else w_f32[:n], dtype=np.float32).astype(np.float64)
+    return (x @ w.T).astype(np.float32)
+
+
+def split_hi_lo(w_f32: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """The router's BF16 hi + lo pair (submission.py:1120-1124): hi = BF16(W), lo = BF16(W - hi),
+    both rounded to nearest even; returns their BF16 bits."""
+    w = np.asarray(w_f32, dtype=np.float32)
+    hi = f32_to_bf16(w)
+    lo = f32_to_bf16((w - bf16_to_f32(hi)).astype(np.float32))
+    return hi, lo
+
+
+def check_implementation_f32(x_bits: np.ndarray, w_f32: np.ndarray, out_f32: np.ndarray, n: int | None = None,
+                             tol: float = ROUTER_TOL, ref: np.ndarray | None = None) -> tuple[bool, str, dict]:
+    """reference.py:84-99 for the router: FP32 ``out_f32`` [M, n] against the FP64 reference
+    rounded to FP32 (ROUTER_TOL), then every probe row within PROBE_TOL."""
+    if ref is None:
+        ref = ref_kernel_f32(x_bits, w_f32, n)
+    out = np.asarray(out_f32, dtype=np.float32)
+    ok, msg, stats = compare(out, ref, tol)
+    rows = probe_rows(x_bits)
+    stats["probe_rows"] = int(len(rows))
+    if not ok or not len(rows):
+        return ok, msg, stats
+    d = np.linalg.norm(out[rows].astype(np.float64) - ref[rows].astype(np.float64), axis=-1)
+    r = np.maximum(np.linalg.norm(ref[rows].astype(np.float64), axis=-1), 1e-30)
+    diff = d / r
+    worst = int(diff.argmax())
+    stats["probe_worst"] = float(diff[worst])
+    if diff[worst] > PROBE_TOL:
+        return False, (f"{msg}, but probe row {int(rows[worst])} is off by {diff[worst]:.2e} > {PROBE_TOL:g}"), stats
+    return True, f"{msg}; {len(rows)} probe rows exact to {float(diff.max()):.1e}", stats
+

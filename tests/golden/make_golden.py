@@ -6,6 +6,8 @@ box never runs this file; the tests only read its outputs:
 - contract.json: sha256 of the reference's generate_weights(5151, "cpu") per layer, and, per input
   case (layer, m, seed, dist), sha256 of generate_input(..., device="cpu")["x"] and of
   ref_kernel's BF16 output (reference.py:44-76).
+- router.json: for the FP32 router, sha256 of generate_input x and of ref_kernel's FP32 output per
+  case, the reference's own check verdicts, and sha256 of the BF16 hi + lo pair it builds.
 - codec_ref.json: the reference's nf12_pack_cuda (submission.py:591-626) on each BF16 layer of those
   weights: c0, escape count and sha256 of every plane and escape array.
 - codec_small.npz: a small W with zeros, -0, subnormals, +-inf, NaN and outliers, and the literal
@@ -35,6 +37,8 @@ TEST_CASES = [("qkv_gate", 1, 7001, "normal"), ("pooler", 7, 7007, "normal"), ("
               ("unpooler", 130, 7130, "normal"), ("unpooler", 5, 7005, "normal"),
               ("qkv_gate", 512, 7512, "outliers"), ("unpooler", 1000, 8000, "outliers")]
 SCORED_MS = (1, 8, 16, 32, 128, 256)
+# The router's two harness tests (m 8 normal, m 9 outliers) and its scored shapes.
+ROUTER_CASES = [(8, 7008, "normal"), (9, 7009, "outliers")] + [(m, 8000 + m, "normal") for m in SCORED_MS]
 BF16_LAYERS = ("qkv_gate", "o", "pooler", "unpooler")
 
 
@@ -82,6 +86,23 @@ def main():
         print("nf12", layer, p["c0"], p["escapes"])
     with open(os.path.join(HERE, "codec_ref.json"), "w") as f:
         json.dump(codec, f, indent=1)
+
+    # The FP32 router: its two harness tests and scored shapes (FP32 output), and the BF16 hi + lo
+    # pair the reference builds in prepare (submission.py:1120-1124).
+    router = {"cases": []}
+    for m, seed, dist in ROUTER_CASES:
+        data = R.generate_input(m, "router", seed=seed, dist=dist, device="cpu")
+        ref = R.ref_kernel(data, weights)
+        ok, msg = R.check_implementation(data, ref, weights)
+        router["cases"].append({"m": m, "seed": seed, "dist": dist, "n": data["config"]["n"], "k": data["config"]["k"],
+                                "x": sha(data["x"]), "ref": sha(ref), "ref_dtype": str(ref.dtype),
+                                "probe_rows": int(len(R.probe_rows(data["x"]))), "self_check": [ok, msg]})
+        print("router", m, dist, msg)
+    hi = weights["router"].to(torch.bfloat16)
+    lo = (weights["router"] - hi.float()).to(torch.bfloat16)
+    router["hi"], router["lo"] = sha(hi), sha(lo)
+    with open(os.path.join(HERE, "router.json"), "w") as f:
+        json.dump(router, f, indent=1)
 
     # A small W with special values, packed by the reference.
     gen = torch.Generator(device="cpu").manual_seed(1234)

@@ -52,6 +52,18 @@ def test_proj_argument_errors_before_any_device_work():
     assert lib.muse_proj_12b_tiles(ctypes.byref(enc), None, 16, 16, 1, ctypes.byref(t12), None, 0, None) == -1
     assert lib.muse_proj_12b_tiles(ctypes.byref(enc), 16, 18, 16, 1, ctypes.byref(t12), None, 0, None) == -2
     assert lib.muse_proj_12b_tiles(ctypes.byref(enc), 16, 16, 16, 1, ctypes.byref(plan12), None, 0, None) == -7
+    # FP32 router: sizes, K rule, null / alignment / plan checks before any device work
+    assert lib.muse_router_tiles_bytes(256, 8192, ctypes.byref(b)) == 0 and b.value == 2 * 256 * 16384
+    assert lib.muse_router_tiles_bytes(256, 100, ctypes.byref(b)) == -3
+    assert lib.muse_pack_router(None, 16, 256, 8192, None) == -1
+    assert lib.muse_pack_router(20, 16, 256, 8192, None) == -2
+    f32 = _lib.MusePlan(kernel=_lib.KERNEL_F32_GEMV)
+    assert lib.muse_proj_f32(16, None, 16, 16, 1, 256, 8192, ctypes.byref(f32), None, 0, None) == -1  # FP32 path needs W
+    assert lib.muse_proj_f32(16, 16, 16, 16, 9, 256, 8192, ctypes.byref(f32), None, 0, None) == -3   # M <= 8
+    assert lib.muse_proj_f32(18, 16, 16, 16, 1, 256, 8192, ctypes.byref(f32), None, 0, None) == -2
+    tc = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE)
+    assert lib.muse_proj_f32(16, 16, None, 16, 16, 256, 8192, ctypes.byref(tc), None, 0, None) == -1  # needs tiles
+    assert lib.muse_proj_f32(16, 16, 16, 16, 16, 256, 8192, ctypes.byref(_lib.MusePlan(kernel=5)), None, 0, None) == -7
 
 
 def test_plan_default_without_device():
@@ -75,6 +87,10 @@ def test_plan_default_without_device():
     assert p.kernel == _lib.KERNEL_TC_12B and p.tile_n == 128
     with pytest.raises(_lib.MuseError):
         _lib.plan_default(1, 2304, 1000, weights_12b=True, tiles=True)
+    p = _lib.plan_default(2, 256, 8192, f32=True)
+    assert p.kernel == _lib.KERNEL_F32_GEMV
+    p = _lib.plan_default(9, 256, 8192, f32=True)
+    assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 16 and p.split > 1 and p.flags & _lib.FLAG_GLOBAL_SPLIT
     with pytest.raises(_lib.MuseError):
         _lib.plan_default(0, 10, 10)
 

@@ -72,10 +72,11 @@ def test_kernel_fn_reference_shapes(state, ref_weights, layer, m, seed, dist):
     assert_parity(bits(data["x"]), bits(ref_weights[layer]), y, data["config"]["n"], what=f"{layer} m={m}")
 
 
-def test_router_is_refused(state):
+def test_router_served_in_fp32(state):
+    """The FP32 router goes through kernel_fn too (its own tests: test_gpu_router.py)."""
     x = torch.zeros((1, 8192), dtype=torch.bfloat16, device="cuda")
-    with pytest.raises(NotImplementedError):
-        submission.kernel_fn({"x": x, "config": {"m": 1, "n": 256, "k": 8192, "layer": "router"}}, state)
+    y = submission.kernel_fn({"x": x, "config": {"m": 1, "n": 256, "k": 8192, "layer": "router"}}, state)
+    assert y.dtype == torch.float32 and y.shape == (1, 256) and int(torch.count_nonzero(y)) == 0
 
 
 def _rand_bits(shape, seed, scale=1.0):

@@ -59,6 +59,40 @@ def test_inputs_and_fp64_outputs_match_reference(golden, weights):
     assert checked >= 25
 
 
+def test_router_inputs_fp32_outputs_and_hi_lo_match_reference(weights):
+    """The FP32 router: generate_input x, the FP64-then-FP32 reference output, the reference's
+    own check verdicts on it, and the BF16 hi + lo pair of its prepare step."""
+    with open(os.path.join(GOLD, "router.json")) as f:
+        gold = json.load(f)
+    w = weights["router"].numpy()
+    assert w.dtype == np.float32 and w.shape == (256, 8192)
+    for case in gold["cases"]:
+        data = C.generate_input(case["m"], "router", case["seed"], case["dist"], device="cpu")
+        xb = bits(data["x"])
+        assert sha(xb) == case["x"], case
+        assert len(O.probe_rows(xb)) == case["probe_rows"]
+        ref = O.ref_kernel_f32(xb, w, case["n"])
+        assert ref.dtype == np.float32 and sha(ref) == case["ref"], case
+        ok, _, _ = O.check_implementation_f32(xb, w, ref, case["n"])
+        assert ok == case["self_check"][0]
+    hi, lo = O.split_hi_lo(w)
+    assert sha(hi) == gold["hi"] and sha(lo) == gold["lo"]
+
+
+def test_router_check_rejects_bf16_weights(weights):
+    """The reference's reason for hi + lo: BF16 router weights alone fail the 1e-4 tolerance,
+    hi + lo with FP32 accumulation passes."""
+    w = weights["router"].numpy()
+    data = C.generate_input(16, "router", 8016, "normal", device="cpu")
+    xb = bits(data["x"])
+    x = O.bf16_to_f32(xb).astype(np.float64)
+    hi, lo = O.split_hi_lo(w)
+    out_bf16 = (x @ O.bf16_to_f32(hi).astype(np.float64).T).astype(np.float32)
+    out_hilo = (x @ (O.bf16_to_f32(hi).astype(np.float64) + O.bf16_to_f32(lo).astype(np.float64)).T).astype(np.float32)
+    assert not O.check_implementation_f32(xb, w, out_bf16)[0]
+    assert O.check_implementation_f32(xb, w, out_hilo)[0]
+
+
 def test_reference_codec_matches_nf12_pack(weights):
     with open(os.path.join(GOLD, "codec_ref.json")) as f:
         g = json.load(f)
