@@ -769,20 +769,18 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
     return m <= 8 ? MUSE_OK : fail(MUSE_ERR_SHAPE, "plan_default: 12-bit weights serve M <= 8");
   }
   if (weights == MUSE_WEIGHTS_F32) {
-    // The router: FP32 on CUDA cores up to 8 tokens, BF16 hi + lo tiles (K = 2k) above.
-    if (m <= 8) {
+    // The router (swept on a B200): FP32 on CUDA cores up to 4 tokens; above, the hi | lo tiles
+    // with 16-token tiles and K split so that the grid is about 256 CTAs (at most 16 ways).
+    if (m <= 4) {
       out->kernel = MUSE_KERNEL_F32_GEMV;
       return MUSE_OK;
     }
-    int bnt = 16;
-    while (bnt < m && bnt < 256) bnt *= 2;
     out->kernel = MUSE_KERNEL_TC_TILE;
-    out->tile_n = bnt;
-    const int64_t tiles = ((n + 127) / 128) * ((m + bnt - 1) / bnt);
-    int64_t split = tiles >= sms ? 1 : sms / tiles;
-    split = std::max<int64_t>(1, std::min<int64_t>({split, 32, (2 * k) / 64}));
+    out->tile_n = 16;
+    out->stages = 6;
+    const int64_t tiles = ((n + 127) / 128) * ((m + 15) / 16);
+    const int64_t split = std::max<int64_t>(1, std::min<int64_t>({16, 256 / tiles, (2 * k) / 64}));
     out->split = static_cast<int>(split);
-    out->stages = bnt <= 64 ? 6 : 0;
     if (split > 1) out->flags = MUSE_FLAG_GLOBAL_SPLIT;
     return MUSE_OK;
   }
@@ -1032,12 +1030,22 @@ int muse_proj_f32(const void* x, const float* w, const void* tiles, float* y, in
     const float* wf = w;
     const uint16_t* xb = static_cast<const uint16_t*>(x);
     const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
-    const dim3 grid(static_cast<unsigned>(n));
-    if (m <= 1) muse::router_f32_kernel<1><<<grid, muse::kRouterThreads, 0, st>>>(wf, xb, y, mi, ni, ki);
-    else if (m <= 2) muse::router_f32_kernel<2><<<grid, muse::kRouterThreads, 0, st>>>(wf, xb, y, mi, ni, ki);
-    else if (m <= 4) muse::router_f32_kernel<4><<<grid, muse::kRouterThreads, 0, st>>>(wf, xb, y, mi, ni, ki);
-    else muse::router_f32_kernel<8><<<grid, muse::kRouterThreads, 0, st>>>(wf, xb, y, mi, ni, ki);
-    return launch_error("router_f32 launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(n), 1, 1);
+    cfg.blockDim = dim3(muse::kRouterThreads, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = (plan->flags & MUSE_FLAG_PDL) ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    if (m <= 1) e = cudaLaunchKernelEx(&cfg, muse::router_f32_kernel<1>, wf, xb, y, mi, ni, ki);
+    else if (m <= 2) e = cudaLaunchKernelEx(&cfg, muse::router_f32_kernel<2>, wf, xb, y, mi, ni, ki);
+    else if (m <= 4) e = cudaLaunchKernelEx(&cfg, muse::router_f32_kernel<4>, wf, xb, y, mi, ni, ki);
+    else e = cudaLaunchKernelEx(&cfg, muse::router_f32_kernel<8>, wf, xb, y, mi, ni, ki);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "router_f32 launch: %s", cudaGetErrorString(e));
+    return MUSE_OK;
   }
   if (plan->kernel != MUSE_KERNEL_TC_TILE)
     return fail(MUSE_ERR_PLAN, "proj_f32: plan kernel must be F32_GEMV or TC_TILE");

@@ -10,7 +10,7 @@ table (``dispatch.py``), else by the library's default plan (muse_plan_default):
 - BF16 W, prefill: persistent tcgen05 GEMMs (CTA pairs with cta_group::2 past M = 256);
 - 12-bit W (opt-in or table rows): lossless 12-bit blocks decoded to BF16 in shared memory and fed
   to the tensor cores, or the CUDA-core 12-bit GEMV;
-- the FP32 router: W in FP32 on CUDA cores up to 8 tokens, else its BF16 hi + lo pair as one
+- the FP32 router: W in FP32 on CUDA cores up to 4 tokens, else its BF16 hi + lo pair as one
   K = 2K tensor-core projection with FP32 accumulation and output (submission.py:1027-1076).
 
 All are this build's own sm_100a kernels behind the C ABI in include/muse_proj.h. There is no
@@ -147,7 +147,7 @@ def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | 
                     _known_answer_check(state, name, nn, m)
                     state["checked"].append((name, nn, m))
         for name, w in state["fp32"].items():
-            for m in (1, 8, 9, 16):  # both FP32 plans: CUDA cores up to 8 tokens, hi + lo above
+            for m in (1, 4, 5, 16):  # both FP32 plans: CUDA cores up to 4 tokens, hi + lo above
                 _known_answer_check_f32(state, name, m)
                 state["checked"].append((name, w.shape[0], m))
     torch.cuda.synchronize()

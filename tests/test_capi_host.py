@@ -90,7 +90,9 @@ def test_plan_default_without_device():
     p = _lib.plan_default(2, 256, 8192, f32=True)
     assert p.kernel == _lib.KERNEL_F32_GEMV
     p = _lib.plan_default(9, 256, 8192, f32=True)
-    assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 16 and p.split > 1 and p.flags & _lib.FLAG_GLOBAL_SPLIT
+    assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 16 and p.split == 16 and p.flags & _lib.FLAG_GLOBAL_SPLIT
+    p = _lib.plan_default(256, 256, 8192, f32=True)
+    assert p.split == 8
     with pytest.raises(_lib.MuseError):
         _lib.plan_default(0, 10, 10)
 
