@@ -613,9 +613,15 @@ int sn_shape(bool twelve, int64_t m, int64_t n, int64_t k, const MusePlan& p, Sn
     return fail(MUSE_ERR_PLAN, "%s: tile_n must be 16, 32, 64 or 128 (got %d)", name, bnt);
   const int per_stage = muse::sn_smem(bnt, 1) - muse::sn_smem(bnt, 0);
   const int max_stages = (limit - muse::sn_smem(bnt, 0)) / per_stage;
-  const int stages = p.stages > 0 ? p.stages : std::min(twelve ? 6 : 5, max_stages);
+  // 12-bit: the decoder groups take units in turn, and a stage's successive units must belong to
+  // one group (which handles them in order), or a group could wait on a slot two phases ahead of
+  // its mbarrier: stages is a multiple of the group count.
+  const int groups = twelve ? muse::kSnDecGroups : 1;
+  const int stages = p.stages > 0 ? p.stages : std::min(twelve ? 6 : 5, max_stages) / groups * groups;
   if (stages < 2 || stages > max_stages)
     return fail(MUSE_ERR_PLAN, "%s: %d stages do not fit (max %d)", name, stages, max_stages);
+  if (stages % groups)
+    return fail(MUSE_ERR_PLAN, "%s: stages (%d) must be a multiple of the %d decoder groups", name, stages, groups);
   SnShape sh;
   sh.bnt = bnt;
   sh.stages = stages;

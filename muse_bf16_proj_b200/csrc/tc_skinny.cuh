@@ -34,7 +34,8 @@ constexpr int kSnRows = 256;     // W rows a unit (the UMMA's N)
 constexpr int kSnBTile = 32768;  // 256 x 64 BF16, 128-byte swizzled
 constexpr int kSnAWindow = 16384;  // the 128-row A window the MMA reads from an x stage
 
-__host__ __device__ constexpr int sn_threads(bool twelve) { return twelve ? 448 : 192; }
+constexpr int kSnDecGroups = 3;  // 12-bit: decoder groups of four warps, each on every third unit
+__host__ __device__ constexpr int sn_threads(bool twelve) { return twelve ? 192 + 128 * kSnDecGroups : 192; }
 __host__ __device__ constexpr int sn_xbytes(int bnt) { return bnt * 128; }
 // Layout: x ring | W ring (32 KB stages) | escape areas (12-bit: 2 x 128 B a stage) | barriers.
 // The W ring follows the x ring and is at least 64 KB, so the last x stage's 16 KB A window stays
@@ -67,7 +68,8 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
   constexpr int kBlk = kTwelve ? kT12Block : 16384;  // one 128-row block of a unit
   constexpr uint32_t kIdesc = umma_idesc_bf16(128, kSnRows);
   constexpr uint32_t kCols = 512;  // two 256-column accumulators
-  constexpr int kDecWarps = kTwelve ? 8 : 0;
+  constexpr int kDecWarps = kTwelve ? 4 * kSnDecGroups : 0;
+  constexpr int kEpiCols = kTwelve ? 32 : 64;  // TMEM columns an epilogue load brings in
   extern __shared__ uint8_t smem_raw[];
   const bool tracing = a.trace != nullptr && static_cast<int>(blockIdx.x) < a.trace_cap && threadIdx.x == 64;
   const unsigned long long t_start = tracing ? globaltimer() : 0ull;
@@ -84,7 +86,7 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
   uint64_t* acc_empty = acc_full + 2;              // [2] epilogue warps
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  int* dec_abort = last_flag + 1;  // [2] 12-bit: a decoder group's wait failed; the group stops together
+  int* dec_abort = last_flag + 1;  // [kSnDecGroups] 12-bit: a group's wait failed; the group stops together
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -99,14 +101,13 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&decoded[s], kDecWarps > 0 ? kDecWarps / 2 : 1);  // one decoder group a unit
+      mbar_init(&decoded[s], kTwelve ? 4 : 1);  // one decoder group (four warps) a unit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
     }
-    dec_abort[0] = 0;
-    dec_abort[1] = 0;
+    for (int g2 = 0; g2 < kSnDecGroups; ++g2) dec_abort[g2] = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kCols);
@@ -209,20 +210,27 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
     }
     pdl_launch_dependents();
   } else if (kTwelve && warp >= 6) {
-    // Decoders: two groups of four warps take alternate units (group g: units i with i % 2 == g),
-    // so two units' load / decode / store chains overlap. Thread t of a group decodes row t of
-    // both blocks of its units (rows t and t + 128 of the B tile).
+    // Decoders: kSnDecGroups groups of four warps take units in turn (group g: units i with
+    // i % kSnDecGroups == g), so that many units' load / decode / store chains overlap. Thread t of
+    // a group decodes row t of both blocks of its units (rows t and t + 128 of the B tile).
     const int grp = (warp - 6) >> 2;
     const int t = ((warp - 6) & 3) * 32 + lane;
     const int swz = t & 7;  // (t + 128) % 8 == t % 8
     int* abort_flag = dec_abort + grp;
     Ring rs;
     Pos p = p0;
-    if (grp == 1 && n_units > 0) {
+    for (int j = 0; j < grp && j < n_units; ++j) {
       rs.next(stages);
       step(p);
     }
-    for (int i = grp; i < n_units; i += 2) {
+    // The group's named barrier (ids 2, 3, ...: 0 is __syncthreads, 1 the epilogue's).
+    auto group_bar = [&]() {
+      if (grp == 0) asm volatile("bar.sync 2, 128;" ::: "memory");  // warp-uniform branches
+      else if (grp == 1) asm volatile("bar.sync 3, 128;" ::: "memory");
+      else asm volatile("bar.sync 4, 128;" ::: "memory");
+    };
+    static_assert(kSnDecGroups <= 3, "group_bar names three barriers");
+    for (int i = grp; i < n_units; i += kSnDecGroups) {
       const int s = rs.slot;
       // Every warp of the group passes the group's named barrier on every unit, also after a
       // failed wait: a warp whose wait failed raises the group's abort flag before the barrier
@@ -252,8 +260,7 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
         }
       }
       // 2. The group has read its inputs: overwrite the stage with the BF16 B tile.
-      if (grp == 0) asm volatile("bar.sync 2, 128;" ::: "memory");  // warp-uniform branch
-      else asm volatile("bar.sync 3, 128;" ::: "memory");
+      group_bar();
       const bool abort = *reinterpret_cast<volatile int*>(abort_flag) != 0;
       if (got && !abort) {
 #pragma unroll
@@ -292,8 +299,7 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
         const int ne1 = have1 ? static_cast<int>(areas[32] & 0xFFFFu) : 0;
         const bool listed0 = ne0 > 0 && ne0 <= kT12EscSlots, listed1 = ne1 > 0 && ne1 <= kT12EscSlots;
         if (listed0 || listed1) {
-          if (grp == 0) asm volatile("bar.sync 2, 128;" ::: "memory");  // warp-uniform branch
-          else asm volatile("bar.sync 3, 128;" ::: "memory");
+          group_bar();
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int ne = h == 0 ? (listed0 ? ne0 : 0) : (listed1 ? ne1 : 0);
@@ -309,10 +315,10 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&decoded[s]);
       if (abort) break;
-      rs.next(stages);
-      rs.next(stages);
-      step(p);
-      step(p);
+      for (int j = 0; j < kSnDecGroups; ++j) {
+        rs.next(stages);
+        step(p);
+      }
     }
   } else if (warp >= 2 && warp <= 5) {
     // Epilogue: TMEM lane = token row of the tile, columns = the unit's 256 W rows.
@@ -351,27 +357,29 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
         const bool mine = ml < mvalid;
         float* slot = whole ? nullptr : slots + (static_cast<size_t>(c - first_c) * BNT + ml) * kSnRows;
 #pragma unroll 1
-        for (int c64 = 0; c64 < kSnRows; c64 += 64) {
-          float v[64];
-          tmem_ld64(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kSnRows + c64), v);
+        for (int cc = 0; cc < kSnRows; cc += kEpiCols) {
+          float v[kEpiCols];
+          const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kSnRows + cc);
+          if constexpr (kEpiCols == 64) tmem_ld64(taddr, v);
+          else tmem_ld32(taddr, v);
           if (!mine) continue;
           if (whole) {
-            const int n = n0 + c64;
+            const int n = n0 + cc;
             uint16_t* dst = a.y + static_cast<size_t>(m) * a.N + n;
-            if (a.y_vec && n + 64 <= a.N) {
+            if (a.y_vec && n + kEpiCols <= a.N) {
 #pragma unroll
-              for (int j = 0; j < 64; j += 8)
+              for (int j = 0; j < kEpiCols; j += 8)
                 *reinterpret_cast<uint4*>(dst + j) = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
                                                                 pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
             } else {
 #pragma unroll
-              for (int j = 0; j < 64; ++j)
+              for (int j = 0; j < kEpiCols; ++j)
                 if (n + j < a.N) dst[j] = f32_to_bf16(v[j]);
             }
           } else {
 #pragma unroll
-            for (int j = 0; j < 64; j += 4)
-              __stcg(reinterpret_cast<float4*>(slot + c64 + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+            for (int j = 0; j < kEpiCols; j += 4)
+              __stcg(reinterpret_cast<float4*>(slot + cc + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
           }
         }
       }
@@ -386,7 +394,7 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
           // Sum the contributors' partials in contributor order (deterministic). The tile's valid
           // rows are float4 groups g = row * 64 + col / 4; thread t takes groups t, t + 128, ...,
           // kB at a time with their loads issued together.
-          constexpr int kB = 8;
+          constexpr int kB = kTwelve ? 4 : 8;  // 12-bit: fewer registers (more threads)
           const int groups = mvalid * (kSnRows / 4);
           const float4* part = reinterpret_cast<const float4*>(slots);
           const size_t cstride = static_cast<size_t>(BNT) * (kSnRows / 4);  // float4s between contributors

@@ -50,7 +50,7 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
     while b16 < m and b16 < 128:
         b16 *= 2
     if twelve_ok and k % 512 == 0 and m <= 256:
-        for stages in (0, 4, 6):
+        for stages in (0, 3):  # multiples of the decoder groups
             out.append(("12b", _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, tile_n=b16, ctas=sms, stages=stages)))
     if m <= 256:
         for stages in (0, 4, 6):

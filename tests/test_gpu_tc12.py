@@ -128,16 +128,16 @@ def test_pack_tiles12_layout():
 
 
 @pytest.mark.parametrize("n,k,m,tile_n,ctas,stages,unused", [
-    (200, 1024, 3, 16, 7, 2, 1),
+    (200, 1024, 3, 16, 7, 3, 1),
     (2304, 8192, 1, 16, 0, 0, 0),
-    (2304, 8192, 16, 16, 148, 5, 2),
+    (2304, 8192, 16, 16, 148, 6, 2),
     (1024, 4096, 33, 64, 100, 3, 3),
-    (4096, 8192, 64, 64, 148, 4, 2),
-    (1024, 2048, 130, 128, 64, 4, 2),
+    (4096, 8192, 64, 64, 148, 3, 2),
+    (1024, 2048, 130, 128, 64, 3, 2),
     (512, 1536, 256, 128, 37, 3, 2),
-    (384, 1024, 5, 16, 3, 2, 1),
+    (384, 1024, 5, 16, 3, 3, 1),
     (6144, 4096, 7, 16, 296, 6, 2),
-    (10240, 8192, 1, 16, 148, 4, 3),
+    (10240, 8192, 1, 16, 148, 6, 3),
 ])
 def test_tc12_parity(n, k, m, tile_n, ctas, stages, unused):
     wb = _weights(n, k, n + m)
@@ -206,7 +206,8 @@ def test_tc12_errors():
                             _lib.MusePlan(kernel=_lib.KERNEL_TC_12B), stream())
     scratch = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
     for bad in (_lib.MusePlan(kernel=_lib.KERNEL_TC_12B, tile_n=24), _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, tile_n=256),
-                _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, stages=40), _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, stages=1)):
+                _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, stages=40), _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, stages=1),
+                _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, stages=4)):  # not a multiple of the decoder groups
         with pytest.raises(_lib.MuseError):
             _lib.proj_12b_tiles(view, enc.tiles.data_ptr(), x.data_ptr(), y.data_ptr(), 4, bad, stream(),
                                 scratch.data_ptr(), scratch.numel())
