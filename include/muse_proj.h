@@ -213,6 +213,16 @@ int muse_pack_tiles12(const MuseEnc12* enc, void* tiles12, void* stream);
 int muse_proj_12b_tiles(const MuseEnc12* enc, const void* tiles12, const void* x, void* y, int64_t m,
                         const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream);
 
+/*
+ * y (FP32 [M, N]) = x . W^T from packed BF16 tiles, FP32 accumulation, no rounding to BF16: the
+ * partial a rank of a row-parallel (K-sharded) projection contributes before the reduce-scatter
+ * that sums the ranks (muse_bf16_proj_b200/sharded.py). plan->kernel must be MUSE_KERNEL_TC_TILE;
+ * scratch as in muse_proj_bf16_tiles. No counterpart in the reference (its `o` projection is this
+ * GPU's K slice with BF16 output, reference.py:17; the sum over the TP group happens outside).
+ */
+int muse_proj_bf16_tiles_f32(const void* x, const void* tiles, float* y, int64_t m, int64_t n, int64_t k,
+                             const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream);
+
 /* Device bytes of the router tiles muse_pack_router writes for an FP32 W [N, K]: the packed tiles
  * (muse_pack_tiles layout) of the BF16 matrix [hi | lo] of N rows and 2K columns. */
 int muse_router_tiles_bytes(int64_t n, int64_t k, int64_t* bytes);

@@ -80,6 +80,7 @@ _SIGNATURES = {
     "muse_tiles12_bytes": ([_I64, _I64, ctypes.POINTER(_I64)], _I32),
     "muse_pack_tiles12": ([ctypes.POINTER(MuseEnc12), _P, _P], _I32),
     "muse_proj_12b_tiles": ([ctypes.POINTER(MuseEnc12), _P, _P, _P, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
+    "muse_proj_bf16_tiles_f32": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
     "muse_router_tiles_bytes": ([_I64, _I64, ctypes.POINTER(_I64)], _I32),
     "muse_pack_router": ([_P, _P, _I64, _I64, _P], _I32),
     "muse_proj_f32": ([_P, _P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
@@ -200,6 +201,12 @@ def proj_12b_tiles(enc: MuseEnc12, tiles12_ptr: int, x_ptr: int, y_ptr: int, m: 
                    scratch_ptr: int = 0, scratch_bytes: int = 0) -> None:
     check(load().muse_proj_12b_tiles(ctypes.byref(enc), tiles12_ptr, x_ptr, y_ptr, m, ctypes.byref(plan),
                                      scratch_ptr or None, scratch_bytes, ctypes.c_void_p(stream)))
+
+
+def proj_bf16_tiles_f32(x_ptr: int, tiles_ptr: int, y_ptr: int, m: int, n: int, k: int, plan: MusePlan, stream: int,
+                        scratch_ptr: int = 0, scratch_bytes: int = 0) -> None:
+    check(load().muse_proj_bf16_tiles_f32(x_ptr, tiles_ptr, y_ptr, m, n, k, ctypes.byref(plan), scratch_ptr or None,
+                                          scratch_bytes, ctypes.c_void_p(stream)))
 
 
 def router_tiles_bytes(n: int, k: int) -> int:

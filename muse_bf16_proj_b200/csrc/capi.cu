@@ -995,6 +995,18 @@ int muse_proj_12b_tiles(const MuseEnc12* enc, const void* tiles12, const void* x
                     static_cast<cudaStream_t>(stream));
 }
 
+int muse_proj_bf16_tiles_f32(const void* x, const void* tiles, float* y, int64_t m, int64_t n, int64_t k,
+                             const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream) {
+  muse::clear_error();
+  if (!x || !tiles || !y || !plan) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles_f32: null pointer");
+  if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles_f32: non-positive size");
+  if (!aligned16(x) || !aligned16(tiles) || (reinterpret_cast<uintptr_t>(y) & 3u) || (k * 2) % 16)
+    return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles_f32: x and tiles 16-byte aligned, y 4-byte aligned, K % 8 == 0");
+  if (plan->kernel != MUSE_KERNEL_TC_TILE) return fail(MUSE_ERR_PLAN, "proj_bf16_tiles_f32: plan kernel must be TC_TILE");
+  return run_tc_tile(x, nullptr, tiles, nullptr, m, n, k, *plan, scratch, scratch_bytes,
+                     static_cast<cudaStream_t>(stream), y, 0);
+}
+
 int muse_router_tiles_bytes(int64_t n, int64_t k, int64_t* bytes) {
   muse::clear_error();
   if (!bytes) return fail(MUSE_ERR_INVALID, "router_tiles_bytes: null output");

@@ -26,6 +26,7 @@ instead of serving (the reference instead fell back to Triton/cuBLAS, submission
 
 from __future__ import annotations
 
+import os
 from typing import TypedDict
 
 import numpy as np
@@ -95,10 +96,12 @@ class _Enc12Device:
 
 
 def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | None = None,
-            self_check: bool = True, verbose: bool = True, pdl: bool = True) -> dict:
-    """Builds the state kernel_fn serves from. ``weights``: name -> W [N, K] on the GPU (BF16;
-    FP32 entries are kept but not served). ``encode_12b`` forces (True) or forbids (False) the
-    12-bit copies; None lets the dispatch table decide."""
+            self_check: bool = True, verbose: bool = True, pdl: bool = True, cache_dir: str | None = None) -> dict:
+    """Builds the state kernel_fn serves from. ``weights``: name -> W [N, K] on the GPU (BF16, or
+    FP32 for the router). ``encode_12b`` forces (True) or forbids (False) the 12-bit copies; None
+    lets the dispatch table decide. ``cache_dir`` (or $MUSE_12B_CACHE): where 12-bit encodings are
+    kept between processes (one file per weight, keyed by the weight's hash; a stale or foreign
+    file is ignored and rewritten)."""
     _lib.load()
     disp = dispatch if dispatch is not None else Dispatch()
     state = {"weights": {}, "tiles": {}, "fp32": {}, "fp32_tiles": {}, "enc12": {}, "dispatch": disp, "checked": [],
@@ -129,14 +132,17 @@ def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | 
         widths = [n] + ([UNPOOL_SLICE] if name == "unpooler" and n > UNPOOL_SLICE else [])
         want = encode_12b if encode_12b is not None else any(disp.wants_12b(nn, k) for nn in widths)
         if want and k % codec12.UNIT == 0 and k <= 65536:
-            enc = codec12.encode(_bits(w))  # raises if the round trip is not bit-exact
+            # From cache_dir's file for this exact weight when there is one, else encoded (raises if
+            # the round trip is not bit-exact) and written there for the next process.
+            enc, cached = codec12.encode_cached(_bits(w), cache_dir or os.environ.get("MUSE_12B_CACHE"))
             if enc.escape_fraction > codec12.MAX_ESCAPE_FRACTION:
                 if verbose:
                     print(f"muse: {name}: {enc.escape_fraction:.3%} escapes, kept BF16 only")
             else:
                 state["enc12"][name] = _Enc12Device(enc, w.device)
                 if verbose:
-                    print(f"muse: {name}: 12-bit planes, {enc.n_esc} escapes ({enc.escape_fraction:.4%})")
+                    print(f"muse: {name}: 12-bit planes{' (cached)' if cached else ''}, {enc.n_esc} escapes "
+                          f"({enc.escape_fraction:.4%})")
     state["scratch"] = torch.zeros(SCRATCH_BYTES, dtype=torch.uint8, device=next(iter(state["weights"].values())).device
                                    if state["weights"] else "cuda")
     if self_check:

@@ -399,3 +399,25 @@ def test_tc_gemm_pairs(m, n, k, stages, ctas):
     assert_parity(xb, wb, y, what=f"gemm2 m={m} n={n} k={k} ctas={ctas}")
     y2 = _run_bf16(xb, wb, plan, tiles=True)
     assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+
+
+@pytest.mark.parametrize("m,n,k,tile_n,split", [(1, 8192, 1024, 16, 8), (16, 8192, 1024, 16, 4), (200, 1000, 2048, 256, 1),
+                                                  (33, 640, 4096, 64, 3)])
+def test_proj_bf16_tiles_f32(m, n, k, tile_n, split):
+    """FP32 output of the tile kernel (a row-parallel rank's partial): within FP32 accumulation of
+    the FP64 product, unrounded."""
+    xb, wb = _rand_bits((m, k), 40 + m), _rand_bits((n, k), 41 + n, 0.02)
+    x, w = to_dev(xb), to_dev(wb)
+    t = torch.empty(_lib.tiles_bytes(n, k), dtype=torch.uint8, device="cuda")
+    _lib.pack_tiles(w.data_ptr(), t.data_ptr(), n, k, stream())
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=tile_n, split=split, flags=_lib.FLAG_GLOBAL_SPLIT if split > 1 else 0)
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    sc = scratch_buf()
+    _lib.proj_bf16_tiles_f32(x.data_ptr(), t.data_ptr(), y.data_ptr(), m, n, k, plan, stream(), sc.data_ptr(), sc.numel())
+    torch.cuda.synchronize()
+    assert _lib.device_error(stream()) == 0
+    ref = O.ref_product(xb, wb)
+    got = y.cpu().numpy().astype(np.float64)
+    assert np.isfinite(got).all()
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-5
+

@@ -1,5 +1,6 @@
-"""The N-sharded projection on 2 GPUs with NCCL: each rank runs the sm_100a kernels on its W shard,
-the all-gather rebuilds y, checked against the FP64 oracle. Skipped with fewer than 2 GPUs."""
+"""The sharded projections on 2 GPUs with NCCL, checked against the FP64 oracle: N-sharded (each rank
+runs the sm_100a kernels on its W shard, the all-gather rebuilds y) and K-sharded (FP32 partials,
+reduce-scatter / all-reduce). Skipped with fewer than 2 GPUs."""
 
 import os
 import socket
@@ -44,6 +45,22 @@ def _worker(rank, world, port, results):
             wb = w.view(torch.int16).numpy().view(np.uint16)
             ok, msg, _ = O.check_implementation(xb, wb, yb)
             out[(m, n, k)] = (ok, msg)
+        # Row-parallel: K-sharded FP32 partials, NCCL reduce-scatter, BF16 column slices.
+        from muse_bf16_proj_b200.sharded import RowParallelProjection
+        for m, n, k in ((1, 8192, 2048), (16, 8192, 2048), (200, 4096, 4096)):
+            g = torch.Generator().manual_seed(3 * m + n)
+            w = (torch.randn((n, k), generator=g) * 0.02).to(torch.bfloat16)
+            x = torch.randn((m, k), generator=g).to(torch.bfloat16)
+            rp = RowParallelProjection(w.cuda(), k)
+            y_full = rp.reduce(rp.partial(x.cuda()), scatter=False)
+            y_cols = rp.reduce(rp.partial(x.cuda()))
+            torch.cuda.synchronize()
+            xb = x.view(torch.int16).numpy().view(np.uint16)
+            wb = w.view(torch.int16).numpy().view(np.uint16)
+            ok, msg, _ = O.check_implementation(xb, wb, y_full.cpu().view(torch.int16).numpy().view(np.uint16))
+            per = n // world
+            same = torch.equal(y_cols.cpu().view(torch.int16), y_full.cpu()[:, rank * per:(rank + 1) * per].view(torch.int16))
+            out[("row", m, n, k)] = (ok and same, msg)
         results[rank] = out
     finally:
         dist.destroy_process_group()

@@ -211,3 +211,26 @@ def test_tc12_errors():
         with pytest.raises(_lib.MuseError):
             _lib.proj_12b_tiles(view, enc.tiles.data_ptr(), x.data_ptr(), y.data_ptr(), 4, bad, stream(),
                                 scratch.data_ptr(), scratch.numel())
+
+
+def test_prepare_reuses_the_12bit_cache(tmp_path):
+    """prepare(cache_dir=...) writes the encoding once; a second prepare reads it and serves the
+    same bits."""
+    import os
+    from muse_bf16_proj_b200.dispatch import Dispatch
+    n, k, m = 1024, 4096, 4
+    wb = _weights(n, k, 77)
+    w = to_dev(wb)
+    entries = [{"n": n, "k": k, "m_lo": 1, "m_hi": 8, "weights": "12b", "plan": {"kernel": "tc_12b", "tile_n": 16}}]
+    xb = bits(torch.randn((m, k), generator=torch.Generator().manual_seed(1)).to(torch.bfloat16))
+    x = to_dev(xb)
+    outs = []
+    for _ in range(2):
+        st = submission.prepare({"w": w}, dispatch=Dispatch(entries=entries), encode_12b=True, verbose=False,
+                                cache_dir=str(tmp_path))
+        outs.append(submission.project(x, st, "w").clone())
+    torch.cuda.synchronize()
+    assert len(os.listdir(tmp_path)) == 1
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    ok, msg, _ = O.check_implementation(xb, wb, bits(outs[0]))
+    assert ok, msg

@@ -10,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from muse_bf16_proj_b200.sharded import ShardedProjection, shard_rows
+from muse_bf16_proj_b200.sharded import RowParallelProjection, ShardedProjection, shard_k, shard_rows
 from oracle import contract_ref as O
 
 
@@ -69,3 +69,59 @@ def test_shard_rows():
         shard_rows(100, 3, 0)
     with pytest.raises(ValueError):
         shard_rows(100, 2, 2)
+
+
+def _oracle_partial(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x . W^T in FP64, rounded to FP32: a rank's row-parallel partial."""
+    xb = x.contiguous().view(torch.int16).numpy().view(np.uint16)
+    wb = w.contiguous().view(torch.int16).numpy().view(np.uint16)
+    return torch.from_numpy(O.ref_product(xb, wb).astype(np.float32))
+
+
+def _row_worker(rank, world, port, m, n, k, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(11)
+        w = (torch.randn((n, k), generator=g) * 0.02).to(torch.bfloat16)
+        x = torch.randn((m, k), generator=g).to(torch.bfloat16)
+        rp = RowParallelProjection(w, k, project_fn=_oracle_partial)
+        part = rp.partial(x)
+        assert part.dtype == torch.float32 and part.shape == (m, n)
+        y_cols = rp.reduce(part.clone())
+        y_full = rp.reduce(part.clone(), scatter=False)
+        xb = x.view(torch.int16).numpy().view(np.uint16)
+        wb = w.view(torch.int16).numpy().view(np.uint16)
+        ref = O.ref_kernel(xb, wb)
+        full_bits = y_full.view(torch.int16).numpy().view(np.uint16)
+        ok_full = O.check_implementation(xb, wb, full_bits, ref_bits=ref)[0]
+        rel = O.relative_l2(O.bf16_to_f32(full_bits), O.bf16_to_f32(ref))
+        per = n // world
+        same = torch.equal(y_cols.view(torch.int16), y_full[:, rank * per:(rank + 1) * per].view(torch.int16))
+        results[rank] = (ok_full, rel, same, (rp.k0, rp.k1))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_row_parallel_projection_gloo(world):
+    """K-sharded partials in FP32, summed across ranks, rounded once: within the reference's check
+    and 1e-3 of the FP64 product; the reduce-scatter slice equals the all-reduce's columns."""
+    m, n, k = 6, 64 * world, 128 * world
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    mp.start_processes(_row_worker, args=(world, _free_port(), m, n, k, results), nprocs=world, join=True,
+                       start_method="spawn")
+    for rank in range(world):
+        ok_full, rel, same, (k0, k1) = results[rank]
+        assert ok_full and rel <= 1e-3 and same
+        assert (k0, k1) == (rank * k // world, (rank + 1) * k // world)
+
+
+def test_shard_k():
+    assert shard_k(8192, 8, 7) == (7168, 8192)
+    with pytest.raises(ValueError):
+        shard_k(1000, 2, 0)  # 500 is not a multiple of 64
+
