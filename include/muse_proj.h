@@ -157,6 +157,54 @@ int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stre
 int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
                          const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream);
 
+/* ---- all-gather fused into the projection's epilogue (column-parallel shards over NVLink) ---- */
+
+#define MUSE_MAX_PEERS 8
+#define MUSE_IPC_HANDLE_BYTES 64
+
+/* Each rank's output and control block, as this process sees them (its own and peers' opened
+ * with muse_ipc_open). y[p] is rank p's y_full [M, ldy] BF16; this rank writes its columns
+ * col0 .. col0 + N into every rank's copy. ctl[p] is rank p's control block of
+ * muse_peer_ctl_bytes bytes, 128-byte aligned, zero-filled once before first use. */
+typedef struct MuseGather {
+  void* y[MUSE_MAX_PEERS];
+  void* ctl[MUSE_MAX_PEERS];
+  int32_t world, rank;
+  int64_t ldy, col0;
+} MuseGather;
+
+/* Bytes of one rank's control block (epoch, ticket, arrive and done flags). */
+int muse_peer_ctl_bytes(int64_t* bytes);
+
+/* CUDA IPC handle (MUSE_IPC_HANDLE_BYTES) of the allocation holding device pointer `ptr`, and
+ * ptr's byte offset inside it, for another process on the same node to open. */
+int muse_ipc_export(const void* ptr, void* handle, int64_t* offset);
+
+/* Opens a peer's exported allocation in this process (peer access enabled lazily) and returns
+ * the device pointer at `offset` inside it. Close with muse_ipc_close before the peer frees it. */
+int muse_ipc_open(const void* handle, int64_t offset, void** ptr);
+int muse_ipc_close(void* ptr, int64_t offset);
+
+/*
+ * The column-parallel projection with its all-gather fused into the epilogue: this rank computes
+ * y[:, col0 .. col0 + N) = x . W_shard^T from its packed W shard (muse_pack_tiles) and stores
+ * each finished value into every rank's y_full over NVLink (plain stores to peer memory; no
+ * separate all-gather). A flag barrier in the control blocks orders calls: no rank writes a
+ * peer's buffer before that peer has entered the same call (its earlier work on the stream,
+ * such as reads of the previous output, is done), and the launch completes only once every
+ * rank's slice is in this rank's y_full. Every wait is bounded (1 s); a rank that never joins
+ * makes the others' kernels record MUSE_ERR_TIMEOUT (muse_device_error) instead of hanging.
+ * All ranks must make the same sequence of calls. plan->kernel: MUSE_KERNEL_TC_TILE (decode,
+ * small M; scratch as muse_scratch_bytes) or MUSE_KERNEL_TC_GEMM2 (prefill). ldy, col0, N
+ * multiples of 8; y_full 16-byte aligned.
+ * Replaces the reference's sharded serving pattern in which the unpooler slice and the MLP-up
+ * shards are followed by a separate all-gather (baseline.py:1-11; SGLang's column-parallel
+ * layers); the reference itself runs no collective.
+ */
+int muse_proj_bf16_tiles_gather(const void* x, const void* tiles, int64_t m, int64_t n, int64_t k,
+                                const MuseGather* g, const MusePlan* plan, void* scratch, int64_t scratch_bytes,
+                                void* stream);
+
 /* Size of the library's built-in scratch area used by muse_proj_bf16_tiles_noalloc. */
 #define MUSE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
 

@@ -61,6 +61,16 @@ class MuseEnc12(ctypes.Structure):
                 ("esc_val", ctypes.c_void_p), ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("n_esc", ctypes.c_int64)]
 
 
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class MuseGather(ctypes.Structure):
+    """Mirror of include/muse_proj.h MuseGather: every rank's y_full and control block."""
+    _fields_ = [("y", ctypes.c_void_p * MAX_PEERS), ("ctl", ctypes.c_void_p * MAX_PEERS), ("world", ctypes.c_int32),
+                ("rank", ctypes.c_int32), ("ldy", ctypes.c_int64), ("col0", ctypes.c_int64)]
+
+
 _lib = None
 
 _P, _I64, _I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
@@ -85,6 +95,12 @@ _SIGNATURES = {
     "muse_pack_router": ([_P, _P, _I64, _I64, _P], _I32),
     "muse_proj_f32": ([_P, _P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P, _I64, _P], _I32),
     "muse_proj_bf16_tiles_noalloc": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P], _I32),
+    "muse_peer_ctl_bytes": ([ctypes.POINTER(_I64)], _I32),
+    "muse_ipc_export": ([_P, _P, ctypes.POINTER(_I64)], _I32),
+    "muse_ipc_open": ([_P, _I64, ctypes.POINTER(_P)], _I32),
+    "muse_ipc_close": ([_P, _I64], _I32),
+    "muse_proj_bf16_tiles_gather": ([_P, _P, _I64, _I64, _I64, ctypes.POINTER(MuseGather), ctypes.POINTER(MusePlan), _P,
+                                     _I64, _P], _I32),
     "muse_encode12_sizes": ([_I64, _I64, ctypes.POINTER(_I64), ctypes.POINTER(_I64)], _I32),
     "muse_encode12": ([_P, _I64, _I64, _P, _P, _P, _P, _I64, ctypes.POINTER(_I64), _I32], _I32),
     "muse_decode12": ([_P, _P, _P, _P, _I64, _I64, _P, _I32], _I32),
@@ -223,6 +239,39 @@ def proj_f32(x_ptr: int, w_ptr: int, tiles_ptr: int, y_ptr: int, m: int, n: int,
              scratch_ptr: int = 0, scratch_bytes: int = 0) -> None:
     check(load().muse_proj_f32(x_ptr, w_ptr or None, tiles_ptr or None, y_ptr, m, n, k, ctypes.byref(plan),
                                scratch_ptr or None, scratch_bytes, ctypes.c_void_p(stream)))
+
+
+def peer_ctl_bytes() -> int:
+    out = ctypes.c_int64()
+    check(load().muse_peer_ctl_bytes(ctypes.byref(out)))
+    return out.value
+
+
+def ipc_export(ptr: int) -> tuple[bytes, int]:
+    """(CUDA IPC handle of the allocation holding device pointer `ptr`, ptr's offset in it)."""
+    handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    off = ctypes.c_int64()
+    check(load().muse_ipc_export(ptr, handle, ctypes.byref(off)))
+    return handle.raw, off.value
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """A peer process's exported device pointer, opened in this process."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError(f"an IPC handle is {IPC_HANDLE_BYTES} bytes (got {len(handle)})")
+    out = ctypes.c_void_p()
+    check(load().muse_ipc_open(handle, offset, ctypes.byref(out)))
+    return out.value
+
+
+def ipc_close(ptr: int, offset: int) -> None:
+    check(load().muse_ipc_close(ptr, offset))
+
+
+def proj_bf16_tiles_gather(x_ptr: int, tiles_ptr: int, m: int, n: int, k: int, gather: MuseGather, plan: MusePlan,
+                           stream: int, scratch_ptr: int = 0, scratch_bytes: int = 0) -> None:
+    check(load().muse_proj_bf16_tiles_gather(x_ptr, tiles_ptr, m, n, k, ctypes.byref(gather), ctypes.byref(plan),
+                                             scratch_ptr or None, scratch_bytes, ctypes.c_void_p(stream)))
 
 
 TRACE_RECORD_BYTES = 48

@@ -254,10 +254,10 @@ int tc_shape(int64_t m, int64_t n, int64_t k, const MusePlan& p, TcShape* out) {
 
 int64_t tc_scratch_bytes(const TcShape& s) { return s.partial_bytes ? kCounterBytes + s.partial_bytes : 0; }
 
-template <int BNT>
+template <int BNT, bool kGather = false>
 int launch_tc_t(const CUtensorMap& tmw, const CUtensorMap& tmx, const muse::TcArgs& a, int m, int n, bool pdl,
                 cudaStream_t st) {
-  auto kern = muse::tc_tile_kernel<BNT>;
+  auto kern = muse::tc_tile_kernel<BNT, kGather>;
   const int smem = muse::tc_tile_smem(BNT, a.stages);
   static bool configured[kMaxDevices] = {};
   int dev;
@@ -301,7 +301,7 @@ int launch_tc_t(const CUtensorMap& tmw, const CUtensorMap& tmx, const muse::TcAr
 // y32 != nullptr: FP32 output; kx > 0: x has kx columns and W (tiles) 2 * kx (the router's hi | lo).
 int run_tc_tile(const void* x, const void* w, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
                 const MusePlan& p, void* scratch, int64_t scratch_bytes, cudaStream_t st, float* y32 = nullptr,
-                int64_t kx = 0) {
+                int64_t kx = 0, const muse::GatherOut* g = nullptr) {
   TcShape sh;
   if (int rc = tc_shape(m, n, k, p, &sh)) return rc;
   const int64_t need = tc_scratch_bytes(sh);
@@ -331,9 +331,20 @@ int run_tc_tile(const void* x, const void* w, const void* tiles, void* y, int64_
   a.mode = sh.mode | (tiles ? muse::kTcModeTiles : 0);
   a.trace = g_trace.load();
   a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  std::memset(&a.g, 0, sizeof(a.g));
+  if (g) a.g = *g;
   const int mi = static_cast<int>(m), ni = static_cast<int>(n);
   // Programmatic launch only for grids without clusters.
   const bool pdl = (p.flags & MUSE_FLAG_PDL) != 0 && !(sh.split > 1 && !(sh.mode & muse::kTcModeGlobalSplit));
+  if (g) {
+    switch (sh.bnt) {
+      case 16: return launch_tc_t<16, true>(tmw, tmx, a, mi, ni, pdl, st);
+      case 32: return launch_tc_t<32, true>(tmw, tmx, a, mi, ni, pdl, st);
+      case 64: return launch_tc_t<64, true>(tmw, tmx, a, mi, ni, pdl, st);
+      case 128: return launch_tc_t<128, true>(tmw, tmx, a, mi, ni, pdl, st);
+      default: return launch_tc_t<256, true>(tmw, tmx, a, mi, ni, pdl, st);
+    }
+  }
   switch (sh.bnt) {
     case 16: return launch_tc_t<16>(tmw, tmx, a, mi, ni, pdl, st);
     case 32: return launch_tc_t<32>(tmw, tmx, a, mi, ni, pdl, st);
@@ -517,8 +528,9 @@ int run_gemm(const void* x, const void* tiles, void* y, int64_t m, int64_t n, in
 
 // ---- persistent prefill GEMM over CTA pairs --------------------------------------------------
 
+// g != nullptr: the all-gather epilogue (y unused; every value goes to each rank's y_full).
 int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p,
-              cudaStream_t st) {
+              cudaStream_t st, const muse::GatherOut* g = nullptr) {
   DeviceInfo* d;
   if (int rc = device_info(&d)) return rc;
   if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
@@ -542,19 +554,21 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   const long long tiles_total = static_cast<long long>(a.mtiles) * a.ntiles;
   const long long tile_rows = static_cast<long long>(a.rtiles) * a.nkb * 128;
   if (tiles_total > INT32_MAX || tile_rows > INT32_MAX) return fail(MUSE_ERR_SHAPE, "tc_gemm2: too many tiles");
+  std::memset(&a.g, 0, sizeof(a.g));
+  if (g) a.g = *g;
   CUtensorMap tmx, tmw;
   if (int rc = make_map(&tmx, x, m, k, 128)) return rc;
   // The packed tile array seen as [tiles * 128 rows, 64] BF16: a box is one 16 KB tile, copied as is.
   if (int rc = make_map(&tmw, tiles, tile_rows, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
-  auto kern = muse::tc_gemm2_kernel;
-  static bool configured[kMaxDevices] = {};
+  auto kern = g ? muse::tc_gemm2_kernel<true> : muse::tc_gemm2_kernel<false>;
+  static bool configured[2][kMaxDevices] = {};
   int dev;
   if (int rc = current_device(&dev)) return rc;
   cudaError_t e = cudaSuccess;
-  if (!configured[dev]) {
+  if (!configured[g ? 1 : 0][dev]) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_gemm2): %s", cudaGetErrorString(e));
-    configured[dev] = true;
+    configured[g ? 1 : 0][dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(muse::kG2Threads, 1, 1);
@@ -1070,6 +1084,99 @@ int muse_proj_f32(const void* x, const float* w, const void* tiles, float* y, in
   if (!tiles) return fail(MUSE_ERR_INVALID, "proj_f32: the tensor-core path reads the hi | lo tiles: null pointer");
   if (!aligned16(tiles)) return fail(MUSE_ERR_ALIGN, "proj_f32: tiles must be 16-byte aligned");
   return run_tc_tile(x, nullptr, tiles, nullptr, m, n, 2 * k, *plan, scratch, scratch_bytes, st, y, k);
+}
+
+// ---- all-gather fused into the epilogue: peer buffers over CUDA IPC ------------------------------
+
+int muse_peer_ctl_bytes(int64_t* bytes) {
+  muse::clear_error();
+  if (!bytes) return fail(MUSE_ERR_INVALID, "peer_ctl_bytes: null output");
+  *bytes = static_cast<int64_t>(sizeof(muse::PeerCtl));
+  return MUSE_OK;
+}
+
+int muse_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+  muse::clear_error();
+  if (!ptr || !handle || !offset) return fail(MUSE_ERR_INVALID, "ipc_export: null argument");
+  static PFN_cuMemGetAddressRange_v3020 range_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range_fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(f);
+  });
+  if (!range_fn) return fail(MUSE_ERR_CUDA, "cuMemGetAddressRange entry point not found");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(MUSE_ERR_INVALID, "ipc_export: pointer is not device memory of this process");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  static_assert(sizeof(h) == MUSE_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return MUSE_OK;
+}
+
+int muse_ipc_open(const void* handle, int64_t offset, void** ptr) {
+  muse::clear_error();
+  if (!handle || !ptr || offset < 0) return fail(MUSE_ERR_INVALID, "ipc_open: bad argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  return MUSE_OK;
+}
+
+int muse_ipc_close(void* ptr, int64_t offset) {
+  muse::clear_error();
+  if (!ptr || offset < 0) return fail(MUSE_ERR_INVALID, "ipc_close: bad argument");
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
+int muse_proj_bf16_tiles_gather(const void* x, const void* tiles, int64_t m, int64_t n, int64_t k,
+                                const MuseGather* g, const MusePlan* plan, void* scratch, int64_t scratch_bytes,
+                                void* stream) {
+  muse::clear_error();
+  if (!x || !tiles || !g || !plan) return fail(MUSE_ERR_INVALID, "proj_gather: null argument");
+  if (m <= 0 || n <= 0 || k <= 0) return fail(MUSE_ERR_SHAPE, "proj_gather: m, n, k must be positive");
+  if (k % 8 != 0) return fail(MUSE_ERR_SHAPE, "proj_gather: k must be a multiple of 8");
+  if (!aligned16(x) || !aligned16(tiles)) return fail(MUSE_ERR_ALIGN, "proj_gather: x and tiles must be 16-byte aligned");
+  if (g->world < 1 || g->world > muse::kMaxPeers || g->rank < 0 || g->rank >= g->world)
+    return fail(MUSE_ERR_INVALID, "proj_gather: world must be 1..%d and 0 <= rank < world (got %d, %d)", muse::kMaxPeers,
+                g->world, g->rank);
+  if (g->col0 < 0 || g->ldy < g->col0 + n || g->ldy > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "proj_gather: columns col0 .. col0 + n must lie inside ldy (col0 %lld, n %lld, ldy %lld)",
+                (long long)g->col0, (long long)n, (long long)g->ldy);
+  if (g->ldy % 8 != 0 || g->col0 % 8 != 0 || n % 8 != 0)
+    return fail(MUSE_ERR_SHAPE, "proj_gather: ldy, col0 and n must be multiples of 8");
+  muse::GatherOut go;
+  std::memset(&go, 0, sizeof(go));
+  for (int p = 0; p < g->world; ++p) {
+    if (!g->y[p] || !g->ctl[p]) return fail(MUSE_ERR_INVALID, "proj_gather: rank %d's buffer or control block is null", p);
+    if (!aligned16(g->y[p])) return fail(MUSE_ERR_ALIGN, "proj_gather: rank %d's y_full must be 16-byte aligned", p);
+    if (reinterpret_cast<uintptr_t>(g->ctl[p]) & 127u)
+      return fail(MUSE_ERR_ALIGN, "proj_gather: rank %d's control block must be 128-byte aligned", p);
+    go.y[p] = static_cast<uint16_t*>(g->y[p]);
+    go.ctl[p] = static_cast<muse::PeerCtl*>(g->ctl[p]);
+  }
+  go.P = g->world;
+  go.rank = g->rank;
+  go.ldy = static_cast<int>(g->ldy);
+  go.col0 = static_cast<int>(g->col0);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (plan->kernel == MUSE_KERNEL_TC_GEMM2) return run_gemm2(x, tiles, nullptr, m, n, k, *plan, st, &go);
+  if (plan->kernel == MUSE_KERNEL_TC_TILE)
+    return run_tc_tile(x, nullptr, tiles, nullptr, m, n, k, *plan, scratch, scratch_bytes, st, nullptr, 0, &go);
+  return fail(MUSE_ERR_PLAN, "proj_gather: the fused all-gather runs on the tc_tile or tc_gemm2 kernel (plan kernel %d)",
+              plan->kernel);
 }
 
 }  // extern "C"

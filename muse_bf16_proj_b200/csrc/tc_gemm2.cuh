@@ -16,6 +16,7 @@
 // warps release an accumulator with remote arrives on the even CTA's barrier.
 #pragma once
 
+#include "gather.cuh"
 #include "ptx.cuh"
 #include "tc_gemm.cuh"  // pack_bf16x2
 
@@ -34,8 +35,11 @@ struct G2Args {
   int mtiles, ntiles, nkb, rtiles;  // 256-token tiles, 256-row tiles, k blocks, 128-row packed tiles
   TraceRec* trace;
   int trace_cap;
+  GatherOut g;  // kGather: every value also goes to each rank's y_full (y is unused)
 };
 
+// kGather: the all-gather epilogue of gather.cuh instead of stores into y.
+template <bool kGather>
 __global__ void __launch_bounds__(kG2Threads, 1)
     tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, const G2Args a) {
   constexpr uint32_t kIdesc = umma_idesc_bf16(256, 256);
@@ -87,6 +91,7 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     if (lane == 0) {
       const uint64_t pol = policy_evict_last();  // x and W tiles are re-read by other pairs
       pdl_wait();
+      if constexpr (kGather) gather_announce(a.g, gather_epoch(a.g));  // early, so peers rarely wait
       Ring ring;     // ring position of the next k block
       int issued = 0;
       bool ok = true;
@@ -142,7 +147,8 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const bool vec_ok = (a.N % 8) == 0;
-    bool waited = false;
+    bool waited = false, peers = false;
+    unsigned int epoch = 0u;
     int local = 0;
     for (int t = pair; t < tiles; t += npairs, ++local) {
       const int b = local & 1;
@@ -154,6 +160,10 @@ __global__ void __launch_bounds__(kG2Threads, 1)
         if (tracing) t_main = globaltimer();
         pdl_wait();
         waited = true;
+        if constexpr (kGather) {
+          epoch = gather_epoch(a.g);
+          peers = gather_arrived(a.g, epoch);
+        }
       }
       if (!ok) break;
       const int m = mt * 256 + static_cast<int>(rank) * 128 + row;
@@ -175,13 +185,20 @@ __global__ void __launch_bounds__(kG2Threads, 1)
             p1.y = pack_bf16x2(v[10], v[11]);
             p1.z = pack_bf16x2(v[12], v[13]);
             p1.w = pack_bf16x2(v[14], v[15]);
-            uint4* dst = reinterpret_cast<uint4*>(yrow + n);
-            dst[0] = p0;
-            dst[1] = p1;
+            if constexpr (kGather) {
+              gather_store16(a.g, peers, m, n, p0, p1);
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(yrow + n);
+              dst[0] = p0;
+              dst[1] = p1;
+            }
           } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (n + j < a.N) yrow[n + j] = f32_to_bf16(v[j]);
+            for (int j = 0; j < 16; ++j) {
+              if (n + j >= a.N) continue;
+              if constexpr (kGather) gather_store(a.g, peers, m, n + j, f32_to_bf16(v[j]));
+              else yrow[n + j] = f32_to_bf16(v[j]);
+            }
           }
         }
       }
@@ -190,11 +207,18 @@ __global__ void __launch_bounds__(kG2Threads, 1)
       if (lane == 0) mbar_arrive_cluster(map_peer(smem_u32(&acc_empty[b]), 0u));
     }
     if (!waited) pdl_wait();
+    if constexpr (kGather) __threadfence_system();  // this thread's stores, before the CTA's ticket
   }
   pdl_launch_dependents();
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (kGather) {
+    if (threadIdx.x == 0) {
+      pdl_wait();
+      gather_finish(a.g, gather_epoch(a.g), gridDim.x);
+    }
+  }
   cluster_sync();  // the pair's UMMAs and both epilogues are done before either CTA frees TMEM
   if (warp == 1) {
     tc_fence_after();

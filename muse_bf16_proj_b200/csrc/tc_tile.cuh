@@ -22,6 +22,7 @@
 // warps 2..5 = epilogue (warp w reads TMEM lanes 32 * (w % 4) .. + 31).
 #pragma once
 
+#include "gather.cuh"
 #include "ptx.cuh"
 
 namespace muse {
@@ -51,6 +52,7 @@ struct TcArgs {
   int M, N, K, split, stages, mode;
   TraceRec* trace;  // optional per-CTA timestamps (nullptr: off)
   int trace_cap;
+  GatherOut g;  // kGather: every value goes to each rank's y_full (y and y32 unused)
 };
 
 // Packed-tile layout: tile (rt, kb) = 16 KB at ((rt * nkb) + kb) * 16384; row r of the tile at
@@ -72,7 +74,8 @@ __global__ void pack_tiles_kernel(const uint16_t* __restrict__ w, uint4* __restr
   }
 }
 
-template <int BNT>
+// kGather: the all-gather epilogue of gather.cuh instead of stores into y.
+template <int BNT, bool kGather = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_tile_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx, const TcArgs a) {
   constexpr int kBBytes = tc_tile_bbytes(BNT);
@@ -95,8 +98,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   float* part = reinterpret_cast<float*>(smem);  // [BNT][128], reuses the ring after the main loop
 
   const bool tiles_mode = (a.mode & kTcModeTiles) != 0;
+  bool peers = false;       // kGather: every rank arrived, so peers' buffers may be written
+  unsigned int epoch = 0u;  // kGather: this call's epoch (read after the programmatic-launch wait)
   auto store = [&](int m, int n, float v) {  // y[m, n] in the output's precision
-    if (a.y32 != nullptr) a.y32[static_cast<size_t>(m) * a.N + n] = v;
+    if constexpr (kGather) gather_store(a.g, peers, m, n, f32_to_bf16(v));
+    else if (a.y32 != nullptr) a.y32[static_cast<size_t>(m) * a.N + n] = v;
     else a.y[static_cast<size_t>(m) * a.N + n] = f32_to_bf16(v);
   };
   const bool global_split = (a.mode & kTcModeGlobalSplit) != 0;
@@ -149,6 +155,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // x's K block for W's K block kb: the same, or kb - kxb past x's end (W = [hi | lo]).
       auto xcol = [&](int kb) { return (a.kxb > 0 && kb >= a.kxb ? kb - a.kxb : kb) * kTcBK; };
       pdl_wait();
+      if constexpr (kGather) gather_announce(a.g, gather_epoch(a.g));  // early, so peers rarely wait
       for (int i = 0; i < pre; ++i)
         tma_load_2d(sb + static_cast<size_t>(i) * kBBytes, &tmx, &full[i], xcol(kb0 + i), tt * BNT, pol_x);
       int issued = pre;
@@ -193,6 +200,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (tracing) t_main = globaltimer();
     pdl_launch_dependents();  // with warps 0 and 1 below: this CTA's loads are done, the next grid may start
     pdl_wait();               // y and the split-K counters may still be in use by the previous grid
+    if constexpr (kGather) {
+      epoch = gather_epoch(a.g);
+      peers = gather_arrived(a.g, epoch);
+    }
     const int tile_id = rt * gridDim.y + tt;
     float* gpart = global_split ? a.partials + (static_cast<size_t>(tile_id) * split + rank) * (BNT * 128) : nullptr;
     if (ok) {
@@ -274,9 +285,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     cluster_sync();  // no CTA leaves while a peer may still read its partial
   }
+  if constexpr (kGather) {
+    if (warp >= 2) __threadfence_system();  // this thread's stores, before the CTA's ticket
+  }
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (kGather) {
+    if (threadIdx.x == 0) {
+      pdl_wait();
+      gather_finish(a.g, gather_epoch(a.g), gridDim.x * gridDim.y);
+    }
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kCols);

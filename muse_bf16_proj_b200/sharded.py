@@ -185,3 +185,140 @@ class RowParallelProjection:
     def reduce(self, y_partial: torch.Tensor, scatter: bool = True) -> torch.Tensor:
         return reduce_columns(y_partial, self.world, self.group, scatter)
 
+
+
+def gather_plan(m: int, n_local: int, k: int, sms: int = 148):
+    """Plan for the fused all-gather projection (``muse_proj_bf16_tiles_gather`` runs the tile
+    kernel or the pair GEMM): above 256 tokens the pair GEMM; else 128-row W tiles x the smallest
+    power-of-two token tile >= M (16 .. 128), K split through scratch so the grid fills the SMs."""
+    from . import _lib as L
+    p = L.MusePlan()
+    if m > 256:
+        p.kernel = L.KERNEL_TC_GEMM2
+        return p
+    tile_n = 16
+    while tile_n < m and tile_n < 128:
+        tile_n *= 2
+    tiles = -(-n_local // 128) * -(-m // tile_n)
+    nkb = -(-k // 64)
+    p.kernel = L.KERNEL_TC_TILE
+    p.tile_n = tile_n
+    p.split = max(1, min(sms // max(tiles, 1), 16, nkb))
+    p.flags = L.FLAG_PDL | (L.FLAG_GLOBAL_SPLIT if p.split > 1 else 0)
+    return p
+
+
+def exchange_peer_entries(entry: dict, group=None) -> list[dict]:
+    """Every rank's ``entry`` (IPC handles and offsets of its output and control block, its device
+    and host), in rank order. Peers must be GPUs of one node: a host mismatch raises."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        return [entry]
+    out = [None] * world
+    dist.all_gather_object(out, entry, group=group)
+    hosts = {e["host"] for e in out}
+    if len(hosts) != 1:
+        raise RuntimeError(f"the fused all-gather needs every rank on one node (hosts {sorted(hosts)})")
+    return out
+
+
+class FusedGatherProjection:
+    """Column-parallel projection whose all-gather is fused into the kernel's epilogue.
+
+    Each rank holds W[r0:r1] (``shard_rows``) as packed tiles and owns y_full [max_rows, N] plus a
+    small control block; the buffers are exchanged once as CUDA IPC handles. ``project(x)`` runs
+    ``muse_proj_bf16_tiles_gather``: the kernel stores every output value of this rank's columns
+    into all ranks' y_full over NVLink as it finishes them, so there is no NCCL step and no
+    staging copy; it returns y_full[:M], complete on this rank's stream when the launch ends.
+    The view is overwritten by the next call; every rank makes the same calls in the same order.
+    """
+
+    def __init__(self, w_full_or_shard: torch.Tensor, n_full: int, max_rows: int, group=None,
+                 shard_given: bool = False):
+        from . import _lib as L
+        import socket
+        self._L = L
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > L.MAX_PEERS:
+            raise ValueError(f"the fused all-gather spans at most {L.MAX_PEERS} ranks (got {self.world})")
+        self.n_full, self.max_rows = n_full, max_rows
+        self.r0, self.r1 = shard_rows(n_full, self.world, self.rank)
+        self.n = self.r1 - self.r0
+        if self.n % 8:
+            raise ValueError(f"each rank's {self.n} columns must be a multiple of 8")
+        shard = w_full_or_shard if shard_given else w_full_or_shard[self.r0:self.r1]
+        if shard.dtype != torch.bfloat16 or not shard.is_cuda or shard.shape[0] != self.n:
+            raise ValueError(f"need a BF16 CUDA shard of {self.n} rows (got {shard.dtype}, {tuple(shard.shape)})")
+        self.k = shard.shape[1]
+        dev = shard.device
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        shard = shard.contiguous()
+        self.tiles = torch.empty(L.tiles_bytes(self.n, self.k), dtype=torch.uint8, device=dev)
+        L.pack_tiles(shard.data_ptr(), self.tiles.data_ptr(), self.n, self.k, stream)
+        self.y_full = torch.empty((max_rows, n_full), dtype=torch.bfloat16, device=dev)
+        self.ctl = torch.zeros(L.peer_ctl_bytes(), dtype=torch.uint8, device=dev)
+        self._scratch = torch.zeros(0, dtype=torch.uint8, device=dev)
+        torch.cuda.synchronize(dev)  # buffers zeroed and W packed before any peer can see them
+        yh, yo = L.ipc_export(self.y_full.data_ptr())
+        ch, co = L.ipc_export(self.ctl.data_ptr())
+        entries = exchange_peer_entries({"y": (yh, yo), "ctl": (ch, co), "rank": self.rank,
+                                         "host": socket.gethostname()}, group)
+        self._opened = []  # (pointer, offset) of peers' buffers opened here
+        g = L.MuseGather()
+        g.world, g.rank, g.ldy, g.col0 = self.world, self.rank, n_full, self.r0
+        try:
+            for p, e in enumerate(entries):
+                if p == self.rank:
+                    g.y[p], g.ctl[p] = self.y_full.data_ptr(), self.ctl.data_ptr()
+                    continue
+                for field in ("y", "ctl"):
+                    ptr = L.ipc_open(*e[field])
+                    self._opened.append((ptr, e[field][1]))
+                    if field == "y":
+                        g.y[p] = ptr
+                    else:
+                        g.ctl[p] = ptr
+        except Exception:
+            self._close_opened()
+            raise
+        self.gather = g
+        self._barrier()  # every rank's peers are open before anyone's first call
+
+    def _barrier(self):
+        if self.world > 1:
+            dist.barrier(group=self.group)
+
+    def _close_opened(self):
+        while self._opened:
+            ptr, off = self._opened.pop()
+            self._L.ipc_close(ptr, off)
+
+    def plan(self, m: int):
+        return gather_plan(m, self.n, self.k, self._L.sm_count())
+
+    def project(self, x: torch.Tensor, plan=None) -> torch.Tensor:
+        L = self._L
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != self.k or not x.is_contiguous():
+            raise ValueError(f"x must be a contiguous BF16 [M, {self.k}] tensor")
+        m = x.shape[0]
+        if not 0 < m <= self.max_rows:
+            raise ValueError(f"M={m} outside 1..{self.max_rows} (the y_full buffer's rows)")
+        if not self._opened and self.world > 1:
+            raise RuntimeError("closed")
+        plan = plan or self.plan(m)
+        need = L.scratch_bytes(m, self.n, self.k, plan)
+        if need > self._scratch.numel():
+            self._scratch = torch.zeros(need, dtype=torch.uint8, device=x.device)
+        L.proj_bf16_tiles_gather(x.data_ptr(), self.tiles.data_ptr(), m, self.n, self.k, self.gather, plan,
+                                 torch.cuda.current_stream(x.device).cuda_stream,
+                                 self._scratch.data_ptr() if need else 0, need)
+        return self.y_full[:m]
+
+    def close(self):
+        """Unmaps the peers' buffers (after every rank's work on them has finished)."""
+        torch.cuda.synchronize(self.y_full.device)
+        self._barrier()
+        self._close_opened()
+        self._barrier()  # no rank frees its buffers while a peer still maps them

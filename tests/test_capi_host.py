@@ -126,3 +126,34 @@ def test_committed_table_rows_are_valid():
         assert e["m_lo"] <= e["m_hi"]
         if p.kernel == _lib.KERNEL_GEMV_12B:
             assert e["weights"] == "12b"
+
+
+def test_gather_argument_errors():
+    """The fused all-gather entry point validates its descriptor before touching the GPU."""
+    assert _lib.peer_ctl_bytes() == 384
+    gat = _lib.MuseGather()
+    gat.world, gat.rank, gat.ldy, gat.col0 = 2, 2, 64, 0
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=16, split=1)
+
+    def code():
+        with pytest.raises(_lib.MuseError) as e:
+            _lib.proj_bf16_tiles_gather(16, 16, 1, 64, 64, gat, plan, 0)
+        return e.value.code
+
+    assert code() == -1  # rank >= world
+    gat.rank, gat.col0 = 1, 8
+    assert code() == -3  # columns col0 .. col0 + n past ldy
+    gat.col0, gat.world = 0, 9
+    assert code() == -1  # more ranks than MUSE_MAX_PEERS
+    gat.world = 2
+    assert code() == -1  # null buffers
+    gat.y[0] = gat.y[1] = gat.ctl[0] = gat.ctl[1] = 256
+    gat.ldy = 68
+    assert code() == -3  # ldy not a multiple of 8
+    gat.ldy = 64
+    plan.kernel = _lib.KERNEL_TC_STREAMK
+    assert code() == -7  # the fused epilogue lives in the tile kernel and the pair GEMM only
+    with pytest.raises(_lib.MuseError):
+        _lib.ipc_export(0)
+    with pytest.raises(ValueError):
+        _lib.ipc_open(b"short", 0)

@@ -125,3 +125,51 @@ def test_shard_k():
     with pytest.raises(ValueError):
         shard_k(1000, 2, 0)  # 500 is not a multiple of 64
 
+
+
+def _exchange_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from muse_bf16_proj_b200.sharded import exchange_peer_entries
+        entry = {"y": (bytes([rank]) * 64, 512 * rank), "ctl": (bytes([100 + rank]) * 64, 0), "rank": rank,
+                 "host": "node0"}
+        got = exchange_peer_entries(entry)
+        ok = [e["rank"] for e in got] == list(range(world)) and all(
+            e["y"] == (bytes([q]) * 64, 512 * q) for q, e in enumerate(got))
+        # A rank on another node must be refused on every rank (no IPC across hosts).
+        bad = dict(entry, host="node1" if rank == world - 1 else "node0")
+        try:
+            exchange_peer_entries(bad)
+            refused = False
+        except RuntimeError:
+            refused = True
+        results[rank] = (ok, refused)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_exchange_peer_entries_gloo(world):
+    """The fused all-gather's one-time exchange of IPC handles: every rank gets every rank's entry in
+    rank order, and ranks on different hosts are refused."""
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    mp.start_processes(_exchange_worker, args=(world, _free_port(), results), nprocs=world, join=True,
+                       start_method="spawn")
+    for rank in range(world):
+        assert results[rank] == (True, True), (rank, results[rank])
+
+
+def test_gather_plan():
+    from muse_bf16_proj_b200 import _lib as L
+    from muse_bf16_proj_b200.sharded import gather_plan
+    p = gather_plan(1, 7168, 8192)  # the MLP-up shard at P = 8, decode
+    assert (p.kernel, p.tile_n, p.split) == (L.KERNEL_TC_TILE, 16, 2)
+    assert p.flags == L.FLAG_PDL | L.FLAG_GLOBAL_SPLIT
+    p = gather_plan(16, 512, 4096)  # the unpooler slice: few W tiles, K split 16 ways
+    assert (p.tile_n, p.split) == (16, 16)
+    p = gather_plan(100, 2048, 64)  # K = one block: no split
+    assert (p.tile_n, p.split, p.flags) == (128, 1, L.FLAG_PDL)
+    assert gather_plan(8192, 7168, 8192).kernel == L.KERNEL_TC_GEMM2
