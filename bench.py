@@ -60,7 +60,9 @@ def parse_args():
     ap.add_argument("--workload", default="smallbatch_qkv", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--m", type=int, default=0, help="override M (small-batch sweep)")
-    ap.add_argument("--gather", action="store_true", help="sharded workloads: also all-gather y (NCCL)")
+    ap.add_argument("--gather", default="", choices=["", "nccl", "fused"],
+                    help="sharded workloads: also all-gather y, by NCCL after the projection or fused into its "
+                         "epilogue (stores into every rank's y over NVLink)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--plan", default="", help="JSON plan overriding the dispatch table for this workload")
@@ -263,9 +265,20 @@ def main():
         submission.project(xs[j], state, names[j], n, out=ys[j])
 
     gather_out = None
-    if sharded and args.gather and world > 1:
+    if sharded and args.gather == "nccl" and world > 1:
         from muse_bf16_proj_b200.sharded import gather_columns
         gather_out = torch.empty((m, n_full), dtype=torch.bfloat16, device=dev)
+    fused = None
+    if sharded and args.gather == "fused":
+        from muse_bf16_proj_b200.sharded import FusedGatherProjection
+        fused = FusedGatherProjection(weights[names[0]], n_full, max_rows=m, shard_given=True)
+        plan = fused.plan(m)
+        if any(name not in state["tiles"] for name in names):
+            raise RuntimeError("the fused all-gather needs the packed tiles of every rotating weight")
+
+        def step(i):  # noqa: F811 - the projection with the all-gather in its epilogue
+            j = i % rot
+            fused.project(xs[j], plan=plan, tiles=state["tiles"][names[j]])
 
     # ---- warm-up, clock soak, timed region --------------------------------------------------
     for i in range(max(3, args.warmup)):
@@ -281,7 +294,17 @@ def main():
     sampler.start()
     soak_end = time.perf_counter() + 1.5
     i = 0
-    while time.perf_counter() < soak_end:
+    if world > 1:
+        # Every rank makes the same number of calls (the fused all-gather pairs each rank's call
+        # with its peers'): the soak's length is agreed as a step count, not a deadline.
+        n_soak = torch.tensor([max(32, min(20000, int(1.5 / max(enqueue_s, 1e-6))))], device=dev)
+        dist.all_reduce(n_soak, op=dist.ReduceOp.MIN)
+        for i in range(int(n_soak[0])):
+            step(i)
+            if i % 32 == 31:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+    while world == 1 and time.perf_counter() < soak_end:
         for _ in range(32):
             step(i)
             i += 1
@@ -321,6 +344,8 @@ def main():
     # ---- e2e through kernel_fn with host buffers --------------------------------------------
     e2e = run_e2e(state, names, layer, m, n, k, rot, K, dev, world, bytes_step, flops_step)
 
+    if fused is not None:
+        fused.close()  # every rank: unmap the peers' buffers before any rank frees its own
     if world > 1:
         dist.barrier()
     if rank != 0:
@@ -377,6 +402,19 @@ def main():
     if gather_out is not None:
         line["config"]["all_gather"] = ("NCCL all_gather_into_tensor of y into [P, M, N/P] plus the copy to [M, N] "
                                         "after every step, inside the timed region")
+    if fused is not None:
+        line["config"]["all_gather"] = ("fused into the projection's epilogue: every output value stored into all "
+                                        f"{world} ranks' y [M, N] over NVLink (CUDA IPC peers), flag barrier per call")
+        # The slower of the GEMM and the link: this rank's slice to each of the other ranks.
+        link_bytes = (world - 1) * m * n * 2
+        link_peak = 770.0  # GB/s per direction per GPU, measured peer copy on this pool's B200s
+        t_link = link_bytes / (link_peak * 1e9)
+        t_math = (bytes_step / (peaks["hbm_gbs"] * 1e9)) if hbm_bound else flops_step / (peak * 1e12)
+        line["roofline"]["fused_gather"] = {
+            "nvlink_bytes_per_rank_per_step": link_bytes, "link_peak_gbs": link_peak,
+            "link_achieved_gbs": round(link_bytes / (mean_launch_ms * 1e-3) / 1e9, 1),
+            "target_us": round(max(t_link, t_math) * 1e6, 3),
+            "frac_of_target": round(max(t_link, t_math) / (mean_launch_ms * 1e-3), 4)}
     if world == 1 and not args.no_cpu_baseline:
         cpu = CpuReference(m, n, k)
         sec, calls = cpu.timed(args.cpu_seconds, max_calls=30)

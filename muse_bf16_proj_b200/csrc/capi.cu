@@ -536,7 +536,8 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
     return fail(MUSE_ERR_SHAPE, "tc_gemm2: dimension too large");
   const int limit = std::min(kSmemLimit, d->smem_optin);
-  const int max_stages = (limit - 1024 - 128) / (muse::kG2Stage + 16);
+  const int extra = g ? muse::g2_smem_gather(0) - muse::g2_smem(0) : 0;  // the gather epilogue's staging
+  const int max_stages = (limit - 1024 - 128 - extra) / (muse::kG2Stage + 16);
   const int stages = p.stages > 0 ? p.stages : std::min(6, max_stages);
   if (stages < 2 || stages > max_stages) return fail(MUSE_ERR_PLAN, "tc_gemm2: %d stages do not fit (max %d)", stages, max_stages);
   muse::G2Args a;
@@ -572,7 +573,7 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   }
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(muse::kG2Threads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(muse::g2_smem(stages));
+  cfg.dynamicSmemBytes = static_cast<size_t>(g ? muse::g2_smem_gather(stages) : muse::g2_smem(stages));
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -28,6 +28,10 @@ constexpr int kG2Stage = 2 * kG2Half;          // x half + W half, per CTA
 constexpr uint32_t kG2Cols = 512;
 
 __host__ __device__ constexpr int g2_smem(int stages) { return 1024 + stages * kG2Stage + (2 * stages + 4) * 8 + 16; }
+// The all-gather variant adds a 4 KB staging tile per epilogue warp (32 rows x 64 columns of BF16),
+// so its stores leave as 128-byte row segments instead of 16 bytes on 32 different rows.
+constexpr int kG2GatherStage = 4 * 32 * 128;
+__host__ __device__ constexpr int g2_smem_gather(int stages) { return g2_smem(stages) + 128 + kG2GatherStage; }
 
 struct G2Args {
   uint16_t* y;  // [M, N]
@@ -56,6 +60,7 @@ __global__ void __launch_bounds__(kG2Threads, 1)
   uint64_t* acc_full = empty + stages;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2], used in the even CTA: 4 local + 4 remote arrives
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint4* gather_stage = reinterpret_cast<uint4*>((reinterpret_cast<uintptr_t>(tmem_slot + 1) + 127) & ~uintptr_t(127));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -168,6 +173,41 @@ __global__ void __launch_bounds__(kG2Threads, 1)
       if (!ok) break;
       const int m = mt * 256 + static_cast<int>(rank) * 128 + row;
       const int n0 = nt * 256;
+      if constexpr (kGather) {
+        // 64 columns at a time: this lane's row into the warp's staging tile (16-byte chunk j of
+        // row r at position j ^ (r % 8): conflict-free), then 8 lanes per row write 128-byte
+        // segments of 4 rows per instruction to every rank.
+        uint4* stg = gather_stage + q * 256;
+        const int m0 = m - lane;
+#pragma unroll 1
+        for (int cc = 0; cc < 256; cc += 64) {
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            float v[16];
+            tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * 256 + cc + h * 16), v);
+            uint4 p0, p1;
+            p0 = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                            pack_bf16x2(v[6], v[7]));
+            p1 = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
+                            pack_bf16x2(v[14], v[15]));
+            stg[lane * 8 + ((2 * h) ^ (lane & 7))] = p0;
+            stg[lane * 8 + ((2 * h + 1) ^ (lane & 7))] = p1;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = i * 4 + (lane >> 3), c = lane & 7;
+            const uint4 val = stg[r * 8 + (c ^ (r & 7))];
+            const int n = n0 + cc + c * 8;
+            if (m0 + r < a.M && n < a.N) gather_store8(a.g, peers, m0 + r, n, val);
+          }
+          __syncwarp();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_peer(smem_u32(&acc_empty[b]), 0u));
+        continue;
+      }
       uint16_t* yrow = a.y + static_cast<size_t>(m) * a.N;
 #pragma unroll 1
       for (int c = 0; c < 256; c += 16) {
@@ -185,20 +225,13 @@ __global__ void __launch_bounds__(kG2Threads, 1)
             p1.y = pack_bf16x2(v[10], v[11]);
             p1.z = pack_bf16x2(v[12], v[13]);
             p1.w = pack_bf16x2(v[14], v[15]);
-            if constexpr (kGather) {
-              gather_store16(a.g, peers, m, n, p0, p1);
-            } else {
-              uint4* dst = reinterpret_cast<uint4*>(yrow + n);
-              dst[0] = p0;
-              dst[1] = p1;
-            }
+            uint4* dst = reinterpret_cast<uint4*>(yrow + n);
+            dst[0] = p0;
+            dst[1] = p1;
           } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if (n + j >= a.N) continue;
-              if constexpr (kGather) gather_store(a.g, peers, m, n + j, f32_to_bf16(v[j]));
-              else yrow[n + j] = f32_to_bf16(v[j]);
-            }
+            for (int j = 0; j < 16; ++j)
+              if (n + j < a.N) yrow[n + j] = f32_to_bf16(v[j]);
           }
         }
       }
@@ -207,7 +240,6 @@ __global__ void __launch_bounds__(kG2Threads, 1)
       if (lane == 0) mbar_arrive_cluster(map_peer(smem_u32(&acc_empty[b]), 0u));
     }
     if (!waited) pdl_wait();
-    if constexpr (kGather) __threadfence_system();  // this thread's stores, before the CTA's ticket
   }
   pdl_launch_dependents();
 

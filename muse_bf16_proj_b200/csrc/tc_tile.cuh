@@ -285,9 +285,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     cluster_sync();  // no CTA leaves while a peer may still read its partial
   }
-  if constexpr (kGather) {
-    if (warp >= 2) __threadfence_system();  // this thread's stores, before the CTA's ticket
-  }
 
   tc_fence_before();
   __syncthreads();

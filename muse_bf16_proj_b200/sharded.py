@@ -190,7 +190,9 @@ class RowParallelProjection:
 def gather_plan(m: int, n_local: int, k: int, sms: int = 148):
     """Plan for the fused all-gather projection (``muse_proj_bf16_tiles_gather`` runs the tile
     kernel or the pair GEMM): above 256 tokens the pair GEMM; else 128-row W tiles x the smallest
-    power-of-two token tile >= M (16 .. 128), K split through scratch so the grid fills the SMs."""
+    power-of-two token tile >= M (16 .. 128), K split through scratch. The split is the one whose
+    grid wastes the least of its last wave (two CTAs an SM with the 6-stage ring of 16- and 32-token
+    tiles), each extra split charged 3 % for its partial sums and pipeline fill."""
     from . import _lib as L
     p = L.MusePlan()
     if m > 256:
@@ -201,10 +203,18 @@ def gather_plan(m: int, n_local: int, k: int, sms: int = 148):
         tile_n *= 2
     tiles = -(-n_local // 128) * -(-m // tile_n)
     nkb = -(-k // 64)
+    per_sm = 2 if tile_n <= 32 else 1
+    best, best_cost = 1, None
+    for split in range(1, min(16, nkb) + 1):
+        waves = -(-(tiles * split) // (sms * per_sm))
+        cost = waves / split * (1 + 0.03 * (split - 1))
+        if best_cost is None or cost < best_cost - 1e-9:
+            best, best_cost = split, cost
     p.kernel = L.KERNEL_TC_TILE
     p.tile_n = tile_n
-    p.split = max(1, min(sms // max(tiles, 1), 16, nkb))
-    p.flags = L.FLAG_PDL | (L.FLAG_GLOBAL_SPLIT if p.split > 1 else 0)
+    p.stages = 6 if per_sm == 2 else 0
+    p.split = best
+    p.flags = L.FLAG_PDL | (L.FLAG_GLOBAL_SPLIT if best > 1 else 0)
     return p
 
 
@@ -298,8 +308,14 @@ class FusedGatherProjection:
     def plan(self, m: int):
         return gather_plan(m, self.n, self.k, self._L.sm_count())
 
-    def project(self, x: torch.Tensor, plan=None) -> torch.Tensor:
+    def project(self, x: torch.Tensor, plan=None, tiles: torch.Tensor | None = None) -> torch.Tensor:
+        """y_full[:M] after x . W^T with every rank's columns. `tiles`: packed tiles of another W
+        shard of the same shape (muse_pack_tiles) to use instead of this one's."""
         L = self._L
+        if tiles is None:
+            tiles = self.tiles
+        elif tiles.numel() * tiles.element_size() != self.tiles.numel() or tiles.device != self.tiles.device:
+            raise ValueError("tiles must be a packed shard of the same shape on the same device")
         if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != self.k or not x.is_contiguous():
             raise ValueError(f"x must be a contiguous BF16 [M, {self.k}] tensor")
         m = x.shape[0]
@@ -311,7 +327,7 @@ class FusedGatherProjection:
         need = L.scratch_bytes(m, self.n, self.k, plan)
         if need > self._scratch.numel():
             self._scratch = torch.zeros(need, dtype=torch.uint8, device=x.device)
-        L.proj_bf16_tiles_gather(x.data_ptr(), self.tiles.data_ptr(), m, self.n, self.k, self.gather, plan,
+        L.proj_bf16_tiles_gather(x.data_ptr(), tiles.data_ptr(), m, self.n, self.k, self.gather, plan,
                                  torch.cuda.current_stream(x.device).cuda_stream,
                                  self._scratch.data_ptr() if need else 0, need)
         return self.y_full[:m]
