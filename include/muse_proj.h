@@ -195,8 +195,8 @@ int muse_ipc_close(void* ptr, int64_t offset);
  * rank's slice is in this rank's y_full. Every wait is bounded (1 s); a rank that never joins
  * makes the others' kernels record MUSE_ERR_TIMEOUT (muse_device_error) instead of hanging.
  * All ranks must make the same sequence of calls. plan->kernel: MUSE_KERNEL_TC_TILE (decode,
- * small M; scratch as muse_scratch_bytes) or MUSE_KERNEL_TC_GEMM2 (prefill). ldy, col0, N
- * multiples of 8; y_full 16-byte aligned.
+ * small M; a K split only with MUSE_FLAG_GLOBAL_SPLIT, scratch as muse_scratch_bytes) or
+ * MUSE_KERNEL_TC_GEMM2 (prefill). ldy, col0, N multiples of 8; y_full 16-byte aligned.
  * Replaces the reference's sharded serving pattern in which the unpooler slice and the MLP-up
  * shards are followed by a separate all-gather (baseline.py:1-11; SGLang's column-parallel
  * layers); the reference itself runs no collective.

@@ -1174,8 +1174,11 @@ int muse_proj_bf16_tiles_gather(const void* x, const void* tiles, int64_t m, int
   go.col0 = static_cast<int>(g->col0);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (plan->kernel == MUSE_KERNEL_TC_GEMM2) return run_gemm2(x, tiles, nullptr, m, n, k, *plan, st, &go);
-  if (plan->kernel == MUSE_KERNEL_TC_TILE)
+  if (plan->kernel == MUSE_KERNEL_TC_TILE) {
+    if (plan->split > 1 && !(plan->flags & MUSE_FLAG_GLOBAL_SPLIT))
+      return fail(MUSE_ERR_PLAN, "proj_gather: a K split must go through scratch (MUSE_FLAG_GLOBAL_SPLIT), not a cluster");
     return run_tc_tile(x, nullptr, tiles, nullptr, m, n, k, *plan, scratch, scratch_bytes, st, nullptr, 0, &go);
+  }
   return fail(MUSE_ERR_PLAN, "proj_gather: the fused all-gather runs on the tc_tile or tc_gemm2 kernel (plan kernel %d)",
               plan->kernel);
 }

@@ -50,6 +50,10 @@ __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
   return v;
 }
 
+// Release / acquire fences (lighter than the sequentially consistent __threadfence forms).
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 __device__ __forceinline__ void st_relaxed_sys(unsigned int* p, unsigned int v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -122,12 +126,12 @@ __device__ __forceinline__ void gather_store8(const GatherOut& g, bool peers, in
 // tickets it observed) before it raises this rank's done flag at each peer. One system fence a
 // launch, not one a CTA. `ctas`: the grid's CTA count.
 __device__ __forceinline__ void gather_finish(const GatherOut& g, unsigned int e, unsigned int ctas) {
-  __threadfence();
+  fence_acq_rel_gpu();  // release: this CTA's stores before its ticket
   PeerCtl* mine = g.ctl[g.rank];
   if (atomicAdd(&mine->ticket, 1u) != ctas - 1u) return;
-  __threadfence();
+  fence_acq_rel_gpu();  // acquire: every CTA's stores before what follows
   mine->ticket = 0u;  // the next call starts from 0 (it reads it only after this grid completes)
-  __threadfence_system();
+  fence_acq_rel_sys();  // release at system scope, before the done flags
   for (int p = 0; p < g.P; ++p)
     if (p != g.rank) st_relaxed_sys(&g.ctl[p]->done[g.rank], e);
   gather_wait_all(mine->done, g.P, g.rank, e, kErrPeerDone);

@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* accf = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* epi_abort = last_flag + 1;  // kGather: an epilogue warp's accumulator wait failed
   float* part = reinterpret_cast<float*>(smem);  // [BNT][128], reuses the ring after the main loop
 
   const bool tiles_mode = (a.mode & kTcModeTiles) != 0;
@@ -124,6 +125,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(accf, 1);
+    *epi_abort = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kCols);
@@ -200,18 +202,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (tracing) t_main = globaltimer();
     pdl_launch_dependents();  // with warps 0 and 1 below: this CTA's loads are done, the next grid may start
     pdl_wait();               // y and the split-K counters may still be in use by the previous grid
+    bool ok_all = ok;  // kGather: the same answer in all four warps, which share named barriers below
     if constexpr (kGather) {
       epoch = gather_epoch(a.g);
       peers = gather_arrived(a.g, epoch);
+      if (!ok && lane == 0) *epi_abort = 1;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      ok_all = *reinterpret_cast<volatile int*>(epi_abort) == 0;
     }
+    // kGather: 16 tokens of this tile's 128 W rows through a [16 tokens][128 rows] BF16 staging
+    // tile in the drained ring, then written out as 256-byte token rows (16 lanes a row) to every
+    // rank, instead of 2-byte stores 32 rows apart.
+    auto stage16 = [&](int c, const float (&v)[16]) {
+      uint16_t* stg = reinterpret_cast<uint16_t*>(smem);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) stg[j * 128 + rl] = f32_to_bf16(v[j]);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const int e = static_cast<int>(threadIdx.x) - 64;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int id = e + 128 * i, j = id >> 4, ch = id & 15;
+        const int m = tt * BNT + c + j, nn = rt * 128 + ch * 8;
+        if (m < a.M && nn < a.N)
+          gather_store8(a.g, peers, m, nn, *reinterpret_cast<const uint4*>(stg + j * 128 + ch * 8));
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    };
     const int tile_id = rt * gridDim.y + tt;
     float* gpart = global_split ? a.partials + (static_cast<size_t>(tile_id) * split + rank) * (BNT * 128) : nullptr;
-    if (ok) {
+    if (kGather ? ok_all : ok) {
 #pragma unroll 1
       for (int c = 0; c < BNT; c += 16) {
         float v[16];
         tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c), v);
-        if (split == 1) {
+        if (kGather && split == 1) {
+          stage16(c, v);
+        } else if (split == 1) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = tt * BNT + c + j;
@@ -237,7 +263,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int c = 0; c < BNT && tt * BNT + c < a.M; c += 16) {
           float sum[16];
           sum_partials16(base + c * 128, split, BNT * 128, sum);
-          if (n < a.N) {
+          if constexpr (kGather) {
+            stage16(c, sum);
+          } else if (n < a.N) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int m = tt * BNT + c + j;

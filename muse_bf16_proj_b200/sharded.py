@@ -192,7 +192,8 @@ def gather_plan(m: int, n_local: int, k: int, sms: int = 148):
     kernel or the pair GEMM): above 256 tokens the pair GEMM; else 128-row W tiles x the smallest
     power-of-two token tile >= M (16 .. 128), K split through scratch. The split is the one whose
     grid wastes the least of its last wave (two CTAs an SM with the 6-stage ring of 16- and 32-token
-    tiles), each extra split charged 3 % for its partial sums and pipeline fill."""
+    tiles), each extra split charged 10 % for its partial sums, pipeline fill and ticket (measured
+    on B200 with the all-gather epilogue: 224 tiles at M = 1 run best unsplit, 32 tiles split 8 ways)."""
     from . import _lib as L
     p = L.MusePlan()
     if m > 256:
@@ -207,7 +208,7 @@ def gather_plan(m: int, n_local: int, k: int, sms: int = 148):
     best, best_cost = 1, None
     for split in range(1, min(16, nkb) + 1):
         waves = -(-(tiles * split) // (sms * per_sm))
-        cost = waves / split * (1 + 0.03 * (split - 1))
+        cost = waves / split * (1 + 0.1 * (split - 1))
         if best_cost is None or cost < best_cost - 1e-9:
             best, best_cost = split, cost
     p.kernel = L.KERNEL_TC_TILE
@@ -270,6 +271,7 @@ class FusedGatherProjection:
         self.y_full = torch.empty((max_rows, n_full), dtype=torch.bfloat16, device=dev)
         self.ctl = torch.zeros(L.peer_ctl_bytes(), dtype=torch.uint8, device=dev)
         self._scratch = torch.zeros(0, dtype=torch.uint8, device=dev)
+        self._plans = {}  # M -> (plan, scratch bytes)
         torch.cuda.synchronize(dev)  # buffers zeroed and W packed before any peer can see them
         yh, yo = L.ipc_export(self.y_full.data_ptr())
         ch, co = L.ipc_export(self.ctl.data_ptr())
@@ -323,8 +325,14 @@ class FusedGatherProjection:
             raise ValueError(f"M={m} outside 1..{self.max_rows} (the y_full buffer's rows)")
         if not self._opened and self.world > 1:
             raise RuntimeError("closed")
-        plan = plan or self.plan(m)
-        need = L.scratch_bytes(m, self.n, self.k, plan)
+        if plan is None:
+            cached = self._plans.get(m)
+            if cached is None:
+                p = self.plan(m)
+                cached = self._plans[m] = (p, L.scratch_bytes(m, self.n, self.k, p))
+            plan, need = cached
+        else:
+            need = L.scratch_bytes(m, self.n, self.k, plan)
         if need > self._scratch.numel():
             self._scratch = torch.zeros(need, dtype=torch.uint8, device=x.device)
         L.proj_bf16_tiles_gather(x.data_ptr(), tiles.data_ptr(), m, self.n, self.k, self.gather, plan,

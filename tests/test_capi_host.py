@@ -153,6 +153,8 @@ def test_gather_argument_errors():
     gat.ldy = 64
     plan.kernel = _lib.KERNEL_TC_STREAMK
     assert code() == -7  # the fused epilogue lives in the tile kernel and the pair GEMM only
+    plan.kernel, plan.split = _lib.KERNEL_TC_TILE, 4
+    assert code() == -7  # a cluster K split is refused (scratch split only)
     with pytest.raises(_lib.MuseError):
         _lib.ipc_export(0)
     with pytest.raises(ValueError):

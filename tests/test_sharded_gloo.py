@@ -168,8 +168,8 @@ def test_gather_plan():
     p = gather_plan(1, 7168, 8192)  # the MLP-up shard at P = 8, decode: 56 tiles x 5 fill one wave
     assert (p.kernel, p.tile_n, p.split, p.stages) == (L.KERNEL_TC_TILE, 16, 5, 6)
     assert p.flags == L.FLAG_PDL | L.FLAG_GLOBAL_SPLIT
-    p = gather_plan(1, 28672, 8192)  # P = 2: 224 tiles; 5 splits leave the least of a wave idle
-    assert (p.tile_n, p.split) == (16, 5)
+    p = gather_plan(1, 28672, 8192)  # P = 2: 224 tiles already fill a wave at two CTAs an SM
+    assert (p.tile_n, p.split, p.flags) == (16, 1, L.FLAG_PDL)
     p = gather_plan(16, 512, 4096)  # the unpooler slice: few W tiles, K split 16 ways
     assert (p.tile_n, p.split) == (16, 16)
     p = gather_plan(100, 2048, 64)  # K = one block: no split
