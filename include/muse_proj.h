@@ -40,6 +40,7 @@ extern "C" {
 #define MUSE_KERNEL_TC_12B 7     /* stream-K tcgen05 on 12-bit tiles: W decoded to BF16 in shared memory */
 #define MUSE_KERNEL_TC_SKINNY 8  /* stream-K tcgen05 over packed tiles with W as the B operand (256 W rows an MMA) */
 #define MUSE_KERNEL_F32_GEMV 9   /* FP32 W on CUDA cores (the router), M <= 8 */
+#define MUSE_KERNEL_GEMV_12T 10  /* 12-bit tiles on CUDA cores, decoded in registers, M <= 4 */
 
 /* Plan flags. */
 #define MUSE_FLAG_GLOBAL_SPLIT 1 /* TC_TILE: reduce K-split partials through caller scratch instead of a cluster */

@@ -17,10 +17,11 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 MUSE_OK = 0
 ERRORS = {-1: "INVALID", -2: "ALIGN", -3: "SHAPE", -4: "CAPACITY", -5: "CUDA", -6: "TIMEOUT", -7: "PLAN"}
 KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_GEMM, KERNEL_TC_GEMM2 = 1, 2, 3, 4, 5, 6
-KERNEL_TC_12B, KERNEL_TC_SKINNY, KERNEL_F32_GEMV = 7, 8, 9
+KERNEL_TC_12B, KERNEL_TC_SKINNY, KERNEL_F32_GEMV, KERNEL_GEMV_12T = 7, 8, 9, 10
 KERNEL_NAMES = {KERNEL_GEMV_BF16: "gemv_bf16", KERNEL_GEMV_12B: "gemv_12b", KERNEL_TC_TILE: "tc_tile",
                 KERNEL_TC_STREAMK: "tc_streamk", KERNEL_TC_GEMM: "tc_gemm", KERNEL_TC_GEMM2: "tc_gemm2",
-                KERNEL_TC_12B: "tc_12b", KERNEL_TC_SKINNY: "tc_skinny", KERNEL_F32_GEMV: "f32_gemv"}
+                KERNEL_TC_12B: "tc_12b", KERNEL_TC_SKINNY: "tc_skinny", KERNEL_F32_GEMV: "f32_gemv",
+                KERNEL_GEMV_12T: "gemv_12t"}
 TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_SKINNY, KERNEL_TC_GEMM, KERNEL_TC_GEMM2)
 KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
 FLAG_GLOBAL_SPLIT = 1
@@ -158,8 +159,8 @@ WEIGHTS_ROW_MAJOR, WEIGHTS_12B, WEIGHTS_TILES, WEIGHTS_12B_TILES, WEIGHTS_F32 = 
 
 
 def plan_default(m: int, n: int, k: int, weights_12b: bool = False, tiles: bool = False, f32: bool = False) -> MusePlan:
-    """The library's default plan; weights_12b with tiles means the 12-bit tiles (TC_12B); f32: the
-    router's FP32 W with its hi | lo tiles."""
+    """The library's default plan; weights_12b with tiles means the 12-bit tiles (GEMV_12T up to 4
+    tokens, TC_12B above); f32: the router's FP32 W with its hi | lo tiles."""
     p = MusePlan()
     if f32:
         fmt = WEIGHTS_F32

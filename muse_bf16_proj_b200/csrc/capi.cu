@@ -21,6 +21,7 @@
 #include "tc12.cuh"
 #include "tc_skinny.cuh"
 #include "router.cuh"
+#include "gemv12t.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -695,6 +696,144 @@ int launch_sn_t(const CUtensorMap& tmx, const muse::SnArgs& a, int g, bool pdl, 
 }
 
 // W: packed BF16 tiles (twelve = false) or 12-bit blocks with enc's escape list (twelve = true).
+// ---- 12-bit GEMV on the 12-bit blocks (register decode) --------------------------------------
+
+struct G12Shape {
+  int mt, stages, rtiles, nkb, ctas, ucap, smax;
+  int64_t scratch;
+  int smem;
+};
+
+// CTAs of gemv12t_kernel<mt> an SM's registers hold (queried once per device and token count).
+int g12_reg_limit(int mt) {
+  static int cache[kMaxDevices][3] = {};
+  int dev = 0;
+  if (current_device(&dev) != MUSE_OK) return 6;
+  const int idx = mt == 1 ? 0 : (mt == 2 ? 1 : 2);
+  if (cache[dev][idx] == 0) {
+    cudaFuncAttributes fa;
+    cudaError_t e = mt == 1 ? cudaFuncGetAttributes(&fa, muse::gemv12t_kernel<1>)
+                    : mt == 2 ? cudaFuncGetAttributes(&fa, muse::gemv12t_kernel<2>)
+                              : cudaFuncGetAttributes(&fa, muse::gemv12t_kernel<4>);
+    int lim = 6;
+    if (e == cudaSuccess && fa.numRegs > 0) {
+      const int per_warp = ((fa.numRegs * 32 + 255) / 256) * 256;  // allocated in 256-register units
+      lim = std::max(1, 65536 / (per_warp * (muse::kG12Threads / 32)));
+    }
+    cache[dev][idx] = lim;
+  }
+  return cache[dev][idx];
+}
+
+// Stream-K grid: as many CTAs as stay resident (up to six an SM; the kernel needs about four to
+// hide its latencies), each taking units / ctas consecutive (row tile, k block) units.
+int g12_shape(int64_t m, int64_t n, int64_t k, const MusePlan& p, G12Shape* out) {
+  DeviceInfo* d;
+  int sms = 148, limit = kSmemLimit;
+  if (device_info(&d) == MUSE_OK) {
+    sms = d->sms;
+    limit = std::min(kSmemLimit, d->smem_optin);
+  }
+  muse::clear_error();
+  if (m < 1 || m > 4) return fail(MUSE_ERR_SHAPE, "gemv_12t: M must be 1..4 (got %lld)", (long long)m);
+  if (k % 128 != 0 || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "gemv_12t: K must be a multiple of 128 and N, K < 2^24");
+  G12Shape sh;
+  sh.mt = m == 1 ? 1 : (m == 2 ? 2 : 4);
+  sh.rtiles = static_cast<int>((n + 127) / 128);
+  sh.nkb = static_cast<int>(k / 64);
+  sh.stages = p.stages > 0 ? p.stages : 3;
+  if (sh.stages < 2) return fail(MUSE_ERR_PLAN, "gemv_12t: at least 2 stages");
+  const int64_t units = static_cast<int64_t>(sh.rtiles) * sh.nkb;
+  if (sh.rtiles > kMaxCounters || units > (int64_t(1) << 30)) return fail(MUSE_ERR_SHAPE, "gemv_12t: too many row tiles");
+  int64_t ctas = 0;
+  if (p.ctas > 0) {
+    ctas = std::min<int64_t>(p.ctas, units);
+  } else {
+    for (int per_sm = std::min(6, g12_reg_limit(sh.mt)); per_sm >= 1 && ctas == 0; --per_sm) {
+      const int64_t g = std::min<int64_t>(units, static_cast<int64_t>(per_sm) * sms);
+      const int ucap = static_cast<int>((units + g - 1) / g);
+      const int smem = muse::g12_smem(sh.stages, ucap, sh.mt);
+      if (smem <= limit && 233472 / (smem + 1024) >= per_sm) ctas = g;
+    }
+    if (ctas == 0) ctas = std::min<int64_t>(units, sms);
+  }
+  sh.ctas = static_cast<int>(ctas);
+  sh.ucap = static_cast<int>((units + ctas - 1) / ctas);
+  const int64_t minrange = std::max<int64_t>(1, units / ctas);
+  sh.smax = static_cast<int>((sh.nkb + minrange - 1) / minrange + 1);
+  sh.smem = muse::g12_smem(sh.stages, sh.ucap, sh.mt);
+  if (sh.smem > limit)
+    return fail(MUSE_ERR_PLAN, "gemv_12t: %d stages and x for %d units need %d bytes of shared memory (limit %d)",
+                sh.stages, sh.ucap, sh.smem, limit);
+  sh.scratch = kCounterBytes + static_cast<int64_t>(sh.rtiles) * sh.smax * sh.mt * 128 * 4;
+  *out = sh;
+  return MUSE_OK;
+}
+
+template <int MT>
+int launch_g12_t(const muse::G12Args& a, int smem, unsigned grid, bool pdl, cudaStream_t st) {
+  auto kern = muse::gemv12t_kernel<MT>;
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaError_t e = cudaSuccess;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(gemv_12t): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(muse::kG12Threads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "gemv_12t launch: %s", cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
+int run_gemv12t(const void* tiles12, const MuseEnc12* enc, const void* x, void* y, int64_t m, const MusePlan& p,
+                void* scratch, int64_t scratch_bytes, cudaStream_t st) {
+  G12Shape sh;
+  if (int rc = g12_shape(m, enc->n, enc->k, p, &sh)) return rc;
+  if (sh.scratch > 0 && (!scratch || scratch_bytes < sh.scratch))
+    return fail(MUSE_ERR_CAPACITY, "gemv_12t: %d CTAs need %lld bytes of zeroed scratch (got %lld)", sh.ctas,
+                (long long)sh.scratch, (long long)(scratch ? scratch_bytes : 0));
+  if (sh.scratch > 0 && (reinterpret_cast<uintptr_t>(scratch) & 255u))
+    return fail(MUSE_ERR_ALIGN, "gemv_12t: scratch must be 256-byte aligned");
+  muse::G12Args a;
+  a.blocks = static_cast<const uint8_t*>(tiles12);
+  a.x = static_cast<const uint16_t*>(x);
+  a.y = static_cast<uint16_t*>(y);
+  a.esc_ptr = enc->esc_ptr;
+  a.esc_val = enc->esc_val;
+  a.counters = sh.scratch > 0 ? static_cast<int*>(scratch) : nullptr;
+  a.partials = sh.scratch > 0 ? reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kCounterBytes) : nullptr;
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(enc->n);
+  a.K = static_cast<int>(enc->k);
+  a.nkb = sh.nkb;
+  a.rtiles = sh.rtiles;
+  a.smax = sh.smax;
+  a.ucap = sh.ucap;
+  a.stages = sh.stages;
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  const bool pdl = (p.flags & MUSE_FLAG_PDL) != 0;
+  const unsigned grid = static_cast<unsigned>(sh.ctas);
+  switch (sh.mt) {
+    case 1: return launch_g12_t<1>(a, sh.smem, grid, pdl, st);
+    case 2: return launch_g12_t<2>(a, sh.smem, grid, pdl, st);
+    default: return launch_g12_t<4>(a, sh.smem, grid, pdl, st);
+  }
+}
+
 int run_skinny(bool twelve, const void* w, const MuseEnc12* enc, const void* x, void* y, int64_t m, int64_t n,
                int64_t k, const MusePlan& p, void* scratch, int64_t scratch_bytes, cudaStream_t st) {
   SnShape sh;
@@ -806,8 +945,13 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
     return MUSE_OK;
   }
   if (weights == MUSE_WEIGHTS_12B_TILES) {
-    // Stream-K over the 12-bit blocks: one CTA an SM with a deep ring.
+    // Stream-K over the 12-bit blocks on the tensor cores: one CTA an SM with a deep ring.
     if (k % 512 || k > 65536) return fail(MUSE_ERR_SHAPE, "plan_default: 12-bit tiles need K % 512 == 0, K <= 65536");
+    if (m <= 4) {  // few tokens: CUDA cores decode in registers (gemv12t.cuh)
+      out->kernel = MUSE_KERNEL_GEMV_12T;
+      out->stages = 3;
+      return MUSE_OK;
+    }
     int bnt = 16;
     while (bnt < m && bnt < 128) bnt *= 2;
     out->kernel = MUSE_KERNEL_TC_12B;
@@ -886,6 +1030,12 @@ int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, in
     SkShape sk;
     if (int rc = sk_shape(m, n, k, *plan, &sk)) return rc;
     *bytes = sk.scratch;
+    return MUSE_OK;
+  }
+  if (plan->kernel == MUSE_KERNEL_GEMV_12T) {
+    G12Shape g;
+    if (int rc = g12_shape(m, n, k, *plan, &g)) return rc;
+    *bytes = g.scratch;
     return MUSE_OK;
   }
   if (plan->kernel == MUSE_KERNEL_TC_12B || plan->kernel == MUSE_KERNEL_TC_SKINNY) {
@@ -1005,7 +1155,10 @@ int muse_proj_12b_tiles(const MuseEnc12* enc, const void* tiles12, const void* x
   if (m < 1 || enc->n < 1 || enc->k < 1) return fail(MUSE_ERR_INVALID, "proj_12b_tiles: non-positive size");
   if (!aligned16(x) || !aligned16(tiles12) || (reinterpret_cast<uintptr_t>(y) & 1u))
     return fail(MUSE_ERR_ALIGN, "proj_12b_tiles: x and tiles 16-byte aligned, y 2-byte aligned");
-  if (plan->kernel != MUSE_KERNEL_TC_12B) return fail(MUSE_ERR_PLAN, "proj_12b_tiles: plan kernel must be TC_12B");
+  if (plan->kernel == MUSE_KERNEL_GEMV_12T)
+    return run_gemv12t(tiles12, enc, x, y, m, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
+  if (plan->kernel != MUSE_KERNEL_TC_12B)
+    return fail(MUSE_ERR_PLAN, "proj_12b_tiles: plan kernel must be TC_12B or GEMV_12T");
   return run_skinny(true, tiles12, enc, x, y, m, enc->n, enc->k, *plan, scratch, scratch_bytes,
                     static_cast<cudaStream_t>(stream));
 }

@@ -25,6 +25,15 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// `base` (a __shared__ array) rounded up to kAlign bytes by adding an offset to the array itself, so
+// the compiler still sees a shared-memory pointer and emits ld/st.shared (rounding the address as an
+// integer would turn every access through the result into a slower generic load or store).
+template <int kAlign>
+__device__ __forceinline__ uint8_t* smem_align(uint8_t* base) {
+  const uint32_t a = smem_u32(base);
+  return base + ((kAlign - (a & (kAlign - 1))) & (kAlign - 1));
+}
+
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

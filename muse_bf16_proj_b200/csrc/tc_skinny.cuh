@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(sn_threads(kTwelve), 1)
   const bool tracing = a.trace != nullptr && static_cast<int>(blockIdx.x) < a.trace_cap && threadIdx.x == 64;
   const unsigned long long t_start = tracing ? globaltimer() : 0ull;
   unsigned long long t_ready = 0ull, t_main = 0ull;
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_align<1024>(smem_raw);
   const int stages = a.stages;
   uint8_t* sx = smem;                                      // [stages][BNT x 64 BF16]
   uint8_t* sw = sx + static_cast<size_t>(stages) * kX;     // [stages][32 KB], 1024-aligned

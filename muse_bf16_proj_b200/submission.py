@@ -282,7 +282,7 @@ def project(x: torch.Tensor, state: dict, layer: str, n: int | None = None,
                                                                                 "flags": plan.flags | _lib.FLAG_PDL}))
     y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     stream = torch.cuda.current_stream(x.device).cuda_stream
-    if fmt == "12b" and plan.kernel == _lib.KERNEL_TC_12B:
+    if fmt == "12b" and plan.kernel in (_lib.KERNEL_TC_12B, _lib.KERNEL_GEMV_12T):
         scratch = _scratch_for(state, m, n, k, plan)
         _lib.proj_12b_tiles(enc.view(n), enc.tiles12.data_ptr(), x.data_ptr(), y.data_ptr(), m, plan, stream,
                             scratch.data_ptr() if scratch is not None else 0,

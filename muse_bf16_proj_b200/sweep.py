@@ -49,6 +49,10 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
     b16 = 16
     while b16 < m and b16 < 128:
         b16 *= 2
+    if twelve_ok and k % 512 == 0 and m <= 4:
+        for per_sm in (0, 3, 4, 5, 6):
+            for stages in (3, 4):
+                out.append(("12b", _lib.MusePlan(kernel=_lib.KERNEL_GEMV_12T, ctas=per_sm * sms, stages=stages)))
     if twelve_ok and k % 512 == 0 and m <= 256:
         for stages in (0, 3):  # multiples of the decoder groups
             out.append(("12b", _lib.MusePlan(kernel=_lib.KERNEL_TC_12B, tile_n=b16, ctas=sms, stages=stages)))
@@ -113,7 +117,7 @@ class ShapeBench:
     def launch(self, i: int, m: int, fmt: str, plan: _lib.MusePlan) -> None:
         j = i % self.rot
         st = torch.cuda.current_stream().cuda_stream
-        if fmt == "12b" and plan.kernel == _lib.KERNEL_TC_12B:
+        if fmt == "12b" and plan.kernel in (_lib.KERNEL_TC_12B, _lib.KERNEL_GEMV_12T):
             _lib.proj_12b_tiles(self.enc[j].view(self.n), self.enc[j].tiles12.data_ptr(), self.x[j].data_ptr(),
                                 self.y[j].data_ptr(), m, plan, st, self.scratch.data_ptr(), self.scratch.numel())
         elif fmt == "12b":
@@ -299,7 +303,7 @@ def main():
     only = None
     if args.plan:
         d = json.loads(args.plan)
-        only = [("12b" if d.get("kernel") in ("gemv_12b", "tc_12b") else "bf16", _lib.MusePlan.from_dict(d))]
+        only = [("12b" if d.get("kernel") in ("gemv_12b", "tc_12b", "gemv_12t") else "bf16", _lib.MusePlan.from_dict(d))]
     shapes = []
     for s in args.shapes.split(","):
         if s == "reference":

@@ -82,6 +82,8 @@ def test_plan_default_without_device():
     p = _lib.plan_default(1, 10240, 8192, weights_12b=True)
     assert p.kernel == _lib.KERNEL_GEMV_12B
     p = _lib.plan_default(1, 10240, 8192, weights_12b=True, tiles=True)
+    assert p.kernel == _lib.KERNEL_GEMV_12T and p.stages == 3
+    p = _lib.plan_default(16, 10240, 8192, weights_12b=True, tiles=True)
     assert p.kernel == _lib.KERNEL_TC_12B and p.tile_n == 16 and p.ctas > 0
     p = _lib.plan_default(300, 2304, 8192, weights_12b=True, tiles=True)
     assert p.kernel == _lib.KERNEL_TC_12B and p.tile_n == 128

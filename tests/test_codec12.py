@@ -83,3 +83,23 @@ def test_encoder_rejects_bad_shapes_and_capacity():
     assert b"capacity" in lib.muse_last_error()
     assert lib.muse_encode12(None, 2, 512, planes.ctypes.data, bases.ctypes.data, esc_ptr.ctypes.data,
                              esc_val.ctypes.data, 4, ctypes.byref(n_esc), 1) == -1
+
+
+def test_escapes_are_stored_as_the_placeholder():
+    """An escaped weight's plane bytes are low byte 0 and code 0, so every decoder (the tensor-core
+    path's in-place decode and the register-decoding GEMV's correction) reads it as the tile's
+    placeholder BF16 base << 8 until its true bits are applied."""
+    w = C.generate_baseline_weight("qkv_decode", 12, device="cpu", recipe="inject")
+    wb = w.view(torch.int16).numpy().view(np.uint16)
+    n, k = wb.shape
+    enc = codec12.encode(wb)
+    units = enc.planes.reshape(n, k // 512, 768)
+    low = units[:, :, :512].reshape(n, k)
+    cb = units[:, :, 512:].reshape(n, k // 2)
+    code = np.empty((n, k), dtype=np.uint8)
+    code[:, 0::2] = cb & 15
+    code[:, 1::2] = cb >> 4
+    rows = np.repeat(np.arange(n), np.diff(enc.esc_ptr))
+    ks = (enc.esc_val >> 16).astype(np.int64)
+    assert rows.size > 0
+    assert not low[rows, ks].any() and not code[rows, ks].any()

@@ -163,7 +163,7 @@ def test_tc12_default_plan_and_repeat():
     xb = bits(torch.randn((m, k), generator=torch.Generator().manual_seed(5)).to(torch.bfloat16))
     x = to_dev(xb)
     plan = _lib.plan_default(m, n, k, weights_12b=True, tiles=True)
-    assert plan.kernel == _lib.KERNEL_TC_12B
+    assert plan.kernel == _lib.KERNEL_GEMV_12T
     need = _lib.scratch_bytes(m, n, k, plan)
     scratch = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
     y0 = _run(enc, x, m, plan, scratch)
@@ -234,3 +234,57 @@ def test_prepare_reuses_the_12bit_cache(tmp_path):
     assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
     ok, msg, _ = O.check_implementation(xb, wb, bits(outs[0]))
     assert ok, msg
+
+
+# ---- the CUDA-core 12-bit GEMV (MUSE_KERNEL_GEMV_12T): decode in registers, M <= 4 ----------------
+
+GEMV12T_CASES = [
+    (200, 1024, 3, 0, 0),      # ragged last row tile, the escape-dense block, default grid
+    (2304, 8192, 1, 0, 0),
+    (2304, 8192, 4, 77, 3),    # row tiles shared by up to 3 CTAs at uneven cuts
+    (10240, 8192, 1, 0, 0),    # the 12-bit benchmark shape
+    (10240, 8192, 2, 300, 4),
+    (384, 1024, 1, 3, 2),      # one CTA a row tile: y written directly
+    (1024, 4096, 4, 1000, 3),  # capped at one unit a CTA: 64 contributors a tile
+    (6144, 4096, 2, 0, 3),
+    (130, 512, 1, 5, 2),       # CTAs spanning two row tiles
+]
+
+
+@pytest.mark.parametrize("n,k,m,ctas,stages", GEMV12T_CASES)
+def test_gemv12t_parity(n, k, m, ctas, stages):
+    wb = _weights(n, k, 7 * n + m)
+    enc = _Enc12Tiles(wb)
+    assert enc.host.n_esc > 0
+    xb = bits(torch.randn((m, k), generator=torch.Generator().manual_seed(m + 1)).to(torch.bfloat16))
+    x = to_dev(xb)
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_GEMV_12T, ctas=ctas, stages=stages, flags=_lib.FLAG_PDL)
+    y = _run(enc, x, m, plan)
+    yb = bits(y)
+    ok, msg, _ = O.check_implementation(xb, wb, yb)
+    assert ok, msg
+    rel = O.relative_l2(O.bf16_to_f32(yb), O.bf16_to_f32(O.ref_kernel(xb, wb)))
+    assert rel <= 1e-3, rel
+    # Against a torch FP32 product of the original weights (the codec is lossless): FP32 sums in a
+    # different order, then one BF16 rounding, so every output is within 2^-8 relative of it.
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref = x.float() @ to_dev(wb).float().t()
+    err = (y.float() - ref).abs()
+    assert bool((err <= ref.abs() * 2.0 ** -8 + 1e-6).all()), float((err / (ref.abs() + 1e-6)).max())
+    y2 = _run(enc, x, m, plan)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16)), "not deterministic"
+
+
+def test_gemv12t_default_plan_and_errors():
+    n, k = 1024, 4096
+    wb = _weights(n, k, 11)
+    enc = _Enc12Tiles(wb)
+    for m in (1, 2, 3, 4):
+        plan = _lib.plan_default(m, n, k, weights_12b=True, tiles=True)
+        assert plan.kernel == _lib.KERNEL_GEMV_12T
+    assert _lib.plan_default(5, n, k, weights_12b=True, tiles=True).kernel == _lib.KERNEL_TC_12B
+    x = to_dev(bits(torch.randn((5, k)).to(torch.bfloat16)))
+    with pytest.raises(_lib.MuseError):  # M = 5 is past the GEMV's token count
+        _run(enc, x, 5, _lib.MusePlan(kernel=_lib.KERNEL_GEMV_12T))
+    with pytest.raises(_lib.MuseError):  # a ring needs two stages
+        _run(enc, x, 1, _lib.MusePlan(kernel=_lib.KERNEL_GEMV_12T, stages=1))
