@@ -529,9 +529,23 @@ int run_gemm(const void* x, const void* tiles, void* y, int64_t m, int64_t n, in
 
 // ---- persistent prefill GEMM over CTA pairs --------------------------------------------------
 
+// Stream-K scratch of the pair GEMM: 64 KB of tickets, then the partials of tiles shared by up to
+// smax pairs ([tile][contributor][CTA] of 128 KB). smax is sized for the most pairs the device can
+// run (fewer pairs only lengthen each pair's run, so fewer share a tile).
+int64_t g2_sk_scratch(int64_t m, int64_t n, int64_t k, int sms, int* smax_out) {
+  const int64_t tiles = ((m + 255) / 256) * ((n + 255) / 256);
+  const int64_t nkb = (k + 63) / 64;
+  const int64_t pairs = std::max(1, sms / 2);
+  const int64_t minrange = std::max<int64_t>(1, tiles * nkb / pairs);
+  const int smax = static_cast<int>((nkb + minrange - 1) / minrange + 1);
+  if (smax_out) *smax_out = smax;
+  return kCounterBytes + tiles * smax * 2 * 128 * 256 * 4;
+}
+
 // g != nullptr: the all-gather epilogue (y unused; every value goes to each rank's y_full).
+// MUSE_FLAG_STREAMK: stream-K schedule over scratch (zeroed once; the kernel leaves it zeroed).
 int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p,
-              cudaStream_t st, const muse::GatherOut* g = nullptr) {
+              cudaStream_t st, const muse::GatherOut* g = nullptr, void* scratch = nullptr, int64_t scratch_bytes = 0) {
   DeviceInfo* d;
   if (int rc = device_info(&d)) return rc;
   if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
@@ -558,6 +572,24 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   if (tiles_total > INT32_MAX || tile_rows > INT32_MAX) return fail(MUSE_ERR_SHAPE, "tc_gemm2: too many tiles");
   std::memset(&a.g, 0, sizeof(a.g));
   if (g) a.g = *g;
+  a.streamk = 0;
+  a.smax = 0;
+  a.partials = nullptr;
+  a.counters = nullptr;
+  if (p.flags & MUSE_FLAG_STREAMK) {
+    if (g) return fail(MUSE_ERR_PLAN, "tc_gemm2: the fused all-gather runs the persistent (not stream-K) schedule");
+    int smax = 0;
+    const int64_t need = g2_sk_scratch(m, n, k, d->sms, &smax);
+    if (!scratch || scratch_bytes < need)
+      return fail(MUSE_ERR_CAPACITY, "tc_gemm2: stream-K needs %lld bytes of zeroed scratch (got %lld)", (long long)need,
+                  (long long)(scratch ? scratch_bytes : 0));
+    if (reinterpret_cast<uintptr_t>(scratch) & 255u) return fail(MUSE_ERR_ALIGN, "tc_gemm2: scratch must be 256-byte aligned");
+    if (tiles_total * 2 > kMaxCounters) return fail(MUSE_ERR_SHAPE, "tc_gemm2: too many tiles for stream-K");
+    a.streamk = 1;
+    a.smax = smax;
+    a.counters = static_cast<int*>(scratch);
+    a.partials = reinterpret_cast<float4*>(static_cast<uint8_t*>(scratch) + kCounterBytes);
+  }
   CUtensorMap tmx, tmw;
   if (int rc = make_map(&tmx, x, m, k, 128)) return rc;
   // The packed tile array seen as [tiles * 128 rows, 64] BF16: a box is one 16 KB tile, copied as is.
@@ -591,7 +623,9 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   if (e != cudaSuccess || clusters < 1)
     return fail(MUSE_ERR_PLAN, "tc_gemm2: CTA pairs cannot be scheduled (%s)", e == cudaSuccess ? "occupancy 0" : cudaGetErrorString(e));
   long long pairs = p.ctas > 0 ? p.ctas / 2 : clusters;
-  pairs = std::max<long long>(1, std::min<long long>({pairs, static_cast<long long>(clusters), tiles_total}));
+  // Persistent tiles: no more pairs than tiles. Stream-K: every resident pair (up to one k block each).
+  const long long cap = a.streamk ? tiles_total * a.nkb : tiles_total;
+  pairs = std::max<long long>(1, std::min<long long>({pairs, static_cast<long long>(clusters), cap}));
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   e = cudaLaunchKernelEx(&cfg, kern, tmx, tmw, a);
   if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_gemm2 launch: %s", cudaGetErrorString(e));
@@ -1044,6 +1078,16 @@ int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, in
     *bytes = sn.scratch;
     return MUSE_OK;
   }
+  if (plan->kernel == MUSE_KERNEL_TC_GEMM2) {
+    if (plan->flags & MUSE_FLAG_STREAMK) {
+      DeviceInfo* d;
+      int sms = 148;
+      if (device_info(&d) == MUSE_OK) sms = d->sms;
+      muse::clear_error();
+      *bytes = g2_sk_scratch(m, n, k, sms, nullptr);
+    }
+    return MUSE_OK;
+  }
   if (plan->kernel != MUSE_KERNEL_TC_TILE) return MUSE_OK;
   TcShape sh;
   if (int rc = tc_shape(m, n, k, *plan, &sh)) return rc;
@@ -1063,7 +1107,8 @@ int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, i
   if (plan->kernel == MUSE_KERNEL_TC_SKINNY)
     return run_skinny(false, tiles, nullptr, x, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_GEMM) return run_gemm(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
-  if (plan->kernel == MUSE_KERNEL_TC_GEMM2) return run_gemm2(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
+  if (plan->kernel == MUSE_KERNEL_TC_GEMM2)
+    return run_gemm2(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream), nullptr, scratch, scratch_bytes);
   if (plan->kernel != MUSE_KERNEL_TC_TILE)
     return fail(MUSE_ERR_PLAN, "proj_bf16_tiles: plan kernel must be TC_TILE, TC_STREAMK, TC_SKINNY, TC_GEMM or TC_GEMM2");
   return run_tc_tile(x, nullptr, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));

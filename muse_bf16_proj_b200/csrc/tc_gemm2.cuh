@@ -18,6 +18,7 @@
 
 #include "gather.cuh"
 #include "ptx.cuh"
+#include "tc12.cuh"     // t12_start / t12_owner: stream-K ranges
 #include "tc_gemm.cuh"  // pack_bf16x2
 
 namespace muse {
@@ -27,7 +28,7 @@ constexpr int kG2Half = 16384;                 // 128 rows x 64 k of BF16
 constexpr int kG2Stage = 2 * kG2Half;          // x half + W half, per CTA
 constexpr uint32_t kG2Cols = 512;
 
-__host__ __device__ constexpr int g2_smem(int stages) { return 1024 + stages * kG2Stage + (2 * stages + 4) * 8 + 16; }
+__host__ __device__ constexpr int g2_smem(int stages) { return 1024 + stages * kG2Stage + (2 * stages + 4) * 8 + 32; }
 // The all-gather variant adds a 4 KB staging tile per epilogue warp (32 rows x 64 columns of BF16),
 // so its stores leave as 128-byte row segments instead of 16 bytes on 32 different rows.
 constexpr int kG2GatherStage = 4 * 32 * 128;
@@ -40,6 +41,46 @@ struct G2Args {
   TraceRec* trace;
   int trace_cap;
   GatherOut g;  // kGather: every value also goes to each rank's y_full (y is unused)
+  // Stream-K (streamk != 0): the (tile, k block) units are cut into equal runs, one per pair; a tile
+  // shared by several pairs leaves FP32 partials in `partials` ([tile][contributor][CTA][64][128]
+  // float4: column quad c of row r at c * 128 + r) and its last contributor adds them in order.
+  int streamk, smax;
+  float4* partials;
+  int* counters;  // [tiles][2], zero between launches
+};
+
+// The segments one pair computes, in order: whole tiles pair, pair + npairs, ... (persistent), or
+// under stream-K the pair's run of (tile, k block) units cut at tile boundaries.
+struct G2Segs {
+  long long u, u1;
+  int t, step, tiles, nkb;
+  bool sk;
+  __device__ G2Segs(const G2Args& a, int pair, int npairs) {
+    tiles = a.mtiles * a.ntiles;
+    nkb = a.nkb;
+    sk = a.streamk != 0;
+    t = pair;
+    step = npairs;
+    const long long units = static_cast<long long>(tiles) * nkb;
+    u = sk ? t12_start(pair, units, npairs) : 0;
+    u1 = sk ? t12_start(pair + 1, units, npairs) : 0;
+  }
+  __device__ bool next(int& tile, int& kb0, int& kb1) {
+    if (!sk) {
+      if (t >= tiles) return false;
+      tile = t;
+      kb0 = 0;
+      kb1 = nkb;
+      t += step;
+      return true;
+    }
+    if (u >= u1) return false;
+    tile = static_cast<int>(u / nkb);
+    kb0 = static_cast<int>(u - static_cast<long long>(tile) * nkb);
+    kb1 = static_cast<int>(min(static_cast<long long>(nkb), kb0 + (u1 - u)));
+    u += kb1 - kb0;
+    return true;
+  }
 };
 
 // kGather: the all-gather epilogue of gather.cuh instead of stores into y.
@@ -60,7 +101,8 @@ __global__ void __launch_bounds__(kG2Threads, 1)
   uint64_t* acc_full = empty + stages;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2], used in the even CTA: 4 local + 4 remote arrives
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  uint4* gather_stage = reinterpret_cast<uint4*>((reinterpret_cast<uintptr_t>(tmem_slot + 1) + 127) & ~uintptr_t(127));
+  int* epi_flag = reinterpret_cast<int*>(tmem_slot + 1);  // stream-K: [0] abort, [1] last contributor
+  uint4* gather_stage = reinterpret_cast<uint4*>(smem_align<128>(reinterpret_cast<uint8_t*>(epi_flag + 2)));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -82,6 +124,7 @@ __global__ void __launch_bounds__(kG2Threads, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 8);
     }
+    epi_flag[0] = epi_flag[1] = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, kG2Cols);
@@ -94,18 +137,23 @@ __global__ void __launch_bounds__(kG2Threads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint64_t pol = policy_evict_last();  // x and W tiles are re-read by other pairs
+      // x is re-read by every pair working on its token tile: keep it. W tiles are re-read only when
+      // there are several token tiles; with one (M <= 256) W streams through once.
+      const uint64_t pol = policy_evict_last();
+      const uint64_t pol_w = a.mtiles > 1 ? pol : policy_evict_first();
       pdl_wait();
       if constexpr (kGather) gather_announce(a.g, gather_epoch(a.g));  // early, so peers rarely wait
       Ring ring;     // ring position of the next k block
       int issued = 0;
       bool ok = true;
-      for (int t = pair; t < tiles && ok; t += npairs) {
+      G2Segs segs(a, pair, npairs);
+      int t, kb0, kb1;
+      while (ok && segs.next(t, kb0, kb1)) {
         const int mt = t % a.mtiles, nt = t / a.mtiles;
         const int xrow = mt * 256 + static_cast<int>(rank) * 128;
         int rt = nt * 2 + static_cast<int>(rank);
         if (rt >= a.rtiles) rt = nt * 2;  // past N: a valid tile; its rows are never stored
-        for (int kb = 0; kb < nkb; ++kb, ++issued, ring.next(stages)) {
+        for (int kb = kb0; kb < kb1; ++kb, ++issued, ring.next(stages)) {
           const int s = ring.slot;
           if (!mbar_wait(&empty[s], ring.phase ^ 1u, kErrTcProducer)) {
             ok = false;
@@ -114,7 +162,7 @@ __global__ void __launch_bounds__(kG2Threads, 1)
           if (leader) mbar_expect_tx(&full[s], static_cast<uint32_t>(2 * kG2Stage));
           const uint32_t bar = map_peer(smem_u32(&full[s]), 0u);
           tma_load_2d_pair(sa + static_cast<size_t>(s) * kG2Half, &tmx, bar, kb * 64, xrow, pol);
-          tma_load_2d_pair(sb + static_cast<size_t>(s) * kG2Half, &tmw, bar, 0, (rt * nkb + kb) * 128, pol);
+          tma_load_2d_pair(sb + static_cast<size_t>(s) * kG2Half, &tmw, bar, 0, (rt * nkb + kb) * 128, pol_w);
         }
       }
       // Every load this CTA issued is consumed (and so has landed) once its stage is released.
@@ -126,12 +174,14 @@ __global__ void __launch_bounds__(kG2Threads, 1)
       Ring ring;
       int local = 0;
       bool ok = true;
-      for (int t = pair; t < tiles && ok; t += npairs, ++local) {
+      G2Segs segs(a, pair, npairs);
+      int t, kb0, kb1;
+      for (; ok && segs.next(t, kb0, kb1); ++local) {
         const int b = local & 1;
         ok = mbar_wait(&acc_empty[b], static_cast<uint32_t>((local >> 1) & 1) ^ 1u, kErrTcMma);
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(b * 256);
-        for (int kb = 0; kb < nkb && ok; ++kb, ring.next(stages)) {
+        for (int kb = kb0; kb < kb1 && ok; ++kb, ring.next(stages)) {
           const int s = ring.slot;
           if (!mbar_wait(&full[s], ring.phase, kErrTcMma)) {
             ok = false;
@@ -142,7 +192,7 @@ __global__ void __launch_bounds__(kG2Threads, 1)
           const uint64_t db = umma_desc_sw128(smem_u32(sb + static_cast<size_t>(s) * kG2Half));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16_pair(d, da + 2 * kk, db + 2 * kk, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16_pair(d, da + 2 * kk, db + 2 * kk, kIdesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           umma_commit_pair_mc(&empty[s], 0x3);
         }
         umma_commit_pair_mc(&acc_full[b], 0x3);
@@ -155,12 +205,20 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     bool waited = false, peers = false;
     unsigned int epoch = 0u;
     int local = 0;
-    for (int t = pair; t < tiles; t += npairs, ++local) {
+    G2Segs segs(a, pair, npairs);
+    int t, kb0, kb1;
+    for (; segs.next(t, kb0, kb1); ++local) {
       const int b = local & 1;
       const int mt = t % a.mtiles, nt = t / a.mtiles;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], static_cast<uint32_t>((local >> 1) & 1),
-                                                        kErrTcEpilogue));
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], static_cast<uint32_t>((local >> 1) & 1),
+                                                  kErrTcEpilogue));
       tc_fence_after();
+      if (a.streamk) {
+        // The four epilogue warps take the same named barriers below: agree on one answer first.
+        if (!ok && lane == 0) epi_flag[0] = 1;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        ok = *reinterpret_cast<volatile int*>(&epi_flag[0]) == 0;
+      }
       if (!waited) {
         if (tracing) t_main = globaltimer();
         pdl_wait();
@@ -173,6 +231,72 @@ __global__ void __launch_bounds__(kG2Threads, 1)
       if (!ok) break;
       const int m = mt * 256 + static_cast<int>(rank) * 128 + row;
       const int n0 = nt * 256;
+      if (a.streamk && !(kb0 == 0 && kb1 == nkb)) {
+        // Part of a tile shared with other pairs: park this CTA's 128 x 256 FP32 partial, release
+        // the accumulator, take the tile's ticket; the last contributor adds every partial in
+        // contributor order and stores BF16.
+        const long long units = static_cast<long long>(tiles) * nkb;
+        const int first = t12_owner(static_cast<long long>(t) * nkb, units, npairs);
+        const int nseg = t12_owner(static_cast<long long>(t + 1) * nkb - 1, units, npairs) - first + 1;
+        float4* tp = a.partials + static_cast<size_t>(t) * a.smax * 2 * 64 * 128;  // this tile's partials
+        float4* mine = tp + (static_cast<size_t>(pair - first) * 2 + rank) * 64 * 128;
+#pragma unroll 1
+        for (int c = 0; c < 256; c += 16) {
+          float v[16];
+          tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * 256 + c), v);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            __stcg(mine + (c / 4 + j) * 128 + row, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_peer(smem_u32(&acc_empty[b]), 0u));
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (row == 0) epi_flag[1] = (ticket_acq_rel(a.counters + t * 2 + static_cast<int>(rank)) == nseg - 1) ? 1 : 0;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (epi_flag[1]) {
+          const float4* part = tp + static_cast<size_t>(rank) * 64 * 128 + row;
+          uint16_t* yrow = a.y + static_cast<size_t>(m) * a.N;
+          // 16 column quads at a time with every contributor's 16 loads in flight together, added
+          // in contributor order.
+#pragma unroll 1
+          for (int c0 = 0; c0 < 64; c0 += 16) {
+            float4 sum[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) sum[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+            for (int p = 0; p < nseg; ++p) {
+              float4 v[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = __ldcg(part + (static_cast<size_t>(p) * 2 * 64 + c0 + j) * 128);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                sum[j].x += v[j].x;
+                sum[j].y += v[j].y;
+                sum[j].z += v[j].z;
+                sum[j].w += v[j].w;
+              }
+            }
+            if (m < a.M) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int n = n0 + (c0 + j) * 4;
+                if (vec_ok && n + 4 <= a.N) {
+                  *reinterpret_cast<uint2*>(yrow + n) =
+                      make_uint2(pack_bf16x2(sum[j].x, sum[j].y), pack_bf16x2(sum[j].z, sum[j].w));
+                } else {
+                  const float sv[4] = {sum[j].x, sum[j].y, sum[j].z, sum[j].w};
+                  for (int e = 0; e < 4; ++e)
+                    if (n + e < a.N) yrow[n + e] = f32_to_bf16(sv[e]);
+                }
+              }
+            }
+          }
+          if (row == 0) a.counters[t * 2 + static_cast<int>(rank)] = 0;  // as the next launch expects it
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // epi_flag[1] is rewritten by the next segment
+        continue;
+      }
       if constexpr (kGather) {
         // 64 columns at a time: this lane's row into the warp's staging tile (16-byte chunk j of
         // row r at position j ^ (r % 8): conflict-free), then 8 lanes per row write 128-byte

@@ -81,6 +81,8 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
     if m >= 128:
         out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM)))
         out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2)))
+        if m <= 2048:  # few 256 x 256 tiles: the stream-K schedule keeps every CTA pair busy
+            out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2, flags=_lib.FLAG_STREAMK)))
     if bnt <= 128:
         for stages, ctas in ((4, 2 * sms), (6, sms), (8, sms)):
             if bnt >= 128 and ctas > sms:
@@ -106,7 +108,7 @@ class ShapeBench:
             t = torch.empty(_lib.tiles_bytes(n, k), dtype=torch.uint8, device="cuda")
             _lib.pack_tiles(w.data_ptr(), t.data_ptr(), n, k, st)
             self.tiles.append(t)
-        self.scratch = torch.zeros(64 << 20, dtype=torch.uint8, device="cuda")
+        self.scratch = torch.zeros(128 << 20, dtype=torch.uint8, device="cuda")
         self.enc = []
         if twelve and k % 512 == 0:
             from .submission import _Enc12Device

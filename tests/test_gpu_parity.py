@@ -421,3 +421,41 @@ def test_proj_bf16_tiles_f32(m, n, k, tile_n, split):
     assert np.isfinite(got).all()
     assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-5
 
+
+
+SK_GEMM2_CASES = [
+    (256, 10240, 8192, 0),  # 40 tiles over 74 pairs: the case the schedule is for
+    (300, 2048, 2048, 0),   # ragged M
+    (128, 4096, 4096, 0),
+    (512, 6144, 4096, 0),
+    (1000, 1536, 1024, 20),  # 10 pairs: each pair's run crosses several tiles
+    (256, 256, 8192, 0),     # one tile shared by every pair
+    (600, 300, 4096, 6),     # ragged N (scalar stores)
+]
+
+
+@pytest.mark.parametrize("m,n,k,ctas", SK_GEMM2_CASES)
+def test_tc_gemm_pairs_streamk(m, n, k, ctas):
+    """The pair GEMM on the stream-K schedule (MUSE_FLAG_STREAMK): tiles shared by several pairs are
+    summed from FP32 partials by their last contributor; deterministic, tickets left at zero."""
+    xb, wb = _rand_bits((m, k), 290 + m), _rand_bits((n, k), 295 + n, 0.02)
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2, ctas=ctas, flags=_lib.FLAG_STREAMK)
+    need = _lib.scratch_bytes(m, n, k, plan)
+    assert need > 0
+    sc = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    x, w = to_dev(xb), to_dev(wb)
+    t = torch.empty(_lib.tiles_bytes(n, k), dtype=torch.uint8, device="cuda")
+    _lib.pack_tiles(w.data_ptr(), t.data_ptr(), n, k, stream())
+    ys = []
+    for _ in range(2):
+        y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        _lib.proj_bf16_tiles(x.data_ptr(), t.data_ptr(), y.data_ptr(), m, n, k, plan, stream(), sc.data_ptr(), need)
+        ys.append(y)
+    torch.cuda.synchronize()
+    assert _lib.device_error(stream()) == 0
+    assert_parity(xb, wb, ys[0], what=f"gemm2 stream-K m={m} n={n} k={k} ctas={ctas}")
+    assert torch.equal(ys[0].view(torch.int16), ys[1].view(torch.int16)), "not deterministic"
+    assert int(sc[:65536].view(torch.int32).abs().sum()) == 0, "tickets not left at zero"
+    with pytest.raises(_lib.MuseError):  # scratch too small
+        _lib.proj_bf16_tiles(x.data_ptr(), t.data_ptr(), ys[0].data_ptr(), m, n, k, plan, stream(), sc.data_ptr(),
+                             need - 256)
