@@ -39,7 +39,7 @@ extern "C" {
 #define MUSE_KERNEL_TC_GEMM2 6   /* persistent tcgen05 GEMM on CTA pairs (cta_group::2), 256 x 256 a tile */
 #define MUSE_KERNEL_TC_12B 7     /* stream-K tcgen05 on 12-bit tiles: W decoded to BF16 in shared memory */
 #define MUSE_KERNEL_TC_SKINNY 8  /* stream-K tcgen05 over packed tiles with W as the B operand (256 W rows an MMA) */
-#define MUSE_KERNEL_F32_GEMV 9   /* FP32 W on CUDA cores (the router), M <= 8 */
+#define MUSE_KERNEL_F32_GEMV 9   /* FP32 W on CUDA cores (the router), M <= 32 */
 #define MUSE_KERNEL_GEMV_12T 10  /* 12-bit tiles on CUDA cores, decoded in registers, M <= 4 */
 
 /* Plan flags. */
@@ -289,7 +289,7 @@ int muse_pack_router(const float* w, void* tiles, int64_t n, int64_t k, void* st
 
 /*
  * y = x . W^T for an FP32 W [N, K] (the router): x BF16 [M, K], y FP32 [M, N]. plan->kernel:
- *   MUSE_KERNEL_F32_GEMV: W read in FP32 on CUDA cores, FP32 accumulation, M <= 8 (`tiles` unused);
+ *   MUSE_KERNEL_F32_GEMV: W read in FP32 on CUDA cores, FP32 accumulation, M <= 32 (`tiles` unused);
  *     replaces router_fp32 / _router_fp32_kernel (submission.py:1027-1042, 131-169);
  *   MUSE_KERNEL_TC_TILE: x . hi^T + x . lo^T as one K = 2K tensor-core projection over the tiles of
  *     muse_pack_router, FP32 accumulation and output (`w` unused); split-K plans take scratch as in

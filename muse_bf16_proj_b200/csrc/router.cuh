@@ -1,6 +1,6 @@
 // The FP32 router projection: y[m, n] = sum_k x[m, k] * W[n, k] with W FP32 and y FP32.
 //
-// Few tokens (M <= 8): router_f32_kernel on CUDA cores reads W in FP32 (as the reference's
+// Few tokens (M <= 32): router_f32_kernel on CUDA cores reads W in FP32 (as the reference's
 // _router_fp32_kernel, submission.py:131-169): one CTA per W row, thread t takes k = 4t + 1024j,
 // eight 16-byte loads of W issued together (before the programmatic-launch wait: W is a
 // prepare-time constant) and 8-byte loads of x, FP32 fused multiply-adds, a warp shuffle and a

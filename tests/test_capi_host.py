@@ -59,7 +59,7 @@ def test_proj_argument_errors_before_any_device_work():
     assert lib.muse_pack_router(20, 16, 256, 8192, None) == -2
     f32 = _lib.MusePlan(kernel=_lib.KERNEL_F32_GEMV)
     assert lib.muse_proj_f32(16, None, 16, 16, 1, 256, 8192, ctypes.byref(f32), None, 0, None) == -1  # FP32 path needs W
-    assert lib.muse_proj_f32(16, 16, 16, 16, 9, 256, 8192, ctypes.byref(f32), None, 0, None) == -3   # M <= 8
+    assert lib.muse_proj_f32(16, 16, 16, 16, 33, 256, 8192, ctypes.byref(f32), None, 0, None) == -3   # M <= 32
     assert lib.muse_proj_f32(18, 16, 16, 16, 1, 256, 8192, ctypes.byref(f32), None, 0, None) == -2
     tc = _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE)
     assert lib.muse_proj_f32(16, 16, None, 16, 16, 256, 8192, ctypes.byref(tc), None, 0, None) == -1  # needs tiles
@@ -91,7 +91,8 @@ def test_plan_default_without_device():
         _lib.plan_default(1, 2304, 1000, weights_12b=True, tiles=True)
     p = _lib.plan_default(2, 256, 8192, f32=True)
     assert p.kernel == _lib.KERNEL_F32_GEMV
-    p = _lib.plan_default(9, 256, 8192, f32=True)
+    assert _lib.plan_default(16, 256, 8192, f32=True).kernel == _lib.KERNEL_F32_GEMV
+    p = _lib.plan_default(17, 256, 8192, f32=True)
     assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 16 and p.split == 16 and p.flags & _lib.FLAG_GLOBAL_SPLIT
     p = _lib.plan_default(256, 256, 8192, f32=True)
     assert p.split == 8

@@ -78,7 +78,7 @@ def _run(state, xb, plan):
 
 
 PLANS = [
-    ("f32", 1, {}), ("f32", 2, {}), ("f32", 3, {}), ("f32", 8, {}),
+    ("f32", 1, {}), ("f32", 2, {}), ("f32", 3, {}), ("f32", 8, {}), ("f32", 9, {}), ("f32", 16, {}), ("f32", 32, {}),
     ("tc", 1, {"tile_n": 16, "split": 32, "flags": 1}), ("tc", 8, {"tile_n": 16, "split": 16, "flags": 1}),
     ("tc", 9, {"tile_n": 16, "split": 8, "flags": 1}), ("tc", 33, {"tile_n": 64, "split": 12, "flags": 1}),
     ("tc", 130, {"tile_n": 128, "split": 4, "flags": 1}), ("tc", 300, {"tile_n": 256, "split": 2, "flags": 1}),
