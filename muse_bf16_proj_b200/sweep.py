@@ -291,6 +291,7 @@ def main():
     ap.add_argument("--no-12b", action="store_true")
     ap.add_argument("--out", default="gpurun_out/sweep.json")
     ap.add_argument("--write-table", action="store_true")
+    ap.add_argument("--merge", action="store_true", help="with --write-table / --from-json: replace only the swept shapes")
     ap.add_argument("--plan", default="", help='time only this plan, e.g. {"kernel": "tc_tile", "split": 3}')
     ap.add_argument("--trace", action="store_true", help="also record per-CTA timestamps of each plan")
     ap.add_argument("--flags", type=int, default=0, help="plan flags OR-ed into every candidate (2 = PDL)")
@@ -299,7 +300,7 @@ def main():
     if args.from_json:
         with open(args.from_json) as f:
             done = json.load(f)
-        write_table(done["rows"], done.get("device", "?"), print)
+        write_table(done["rows"], done.get("device", "?"), print, args.merge)
         return
     torch.backends.cuda.matmul.allow_tf32 = False
     only = None
@@ -335,14 +336,26 @@ def main():
         json.dump({"device": torch.cuda.get_device_name(), "sms": sms, "rows": rows,
                    "seconds": time.time() - t0}, f)
     if args.write_table:
-        write_table(rows, torch.cuda.get_device_name(), log)
+        write_table(rows, torch.cuda.get_device_name(), log, args.merge)
 
 
-def write_table(rows, device: str, log) -> None:
-    table = {"generated_by": "python -m muse_bf16_proj_b200.sweep --write-table (or --from-json of its output)",
+def merge_entries(old: list, new: list) -> list:
+    """The committed table's rows with every (N, K) shape that `new` covers replaced by `new`'s rows
+    (a targeted re-sweep updates its shapes and keeps the rest), sorted by shape, format and M."""
+    swept = {(e["n"], e["k"]) for e in new}
+    kept = [e for e in old if (e["n"], e["k"]) not in swept]
+    return sorted(kept + list(new), key=lambda e: (e["n"], e["k"], e.get("weights", "bf16"), e["m_lo"]))
+
+
+def write_table(rows, device: str, log, merge: bool = False) -> None:
+    entries = table_entries(rows)
+    if merge and os.path.exists(TABLE_PATH):
+        with open(TABLE_PATH) as f:
+            entries = merge_entries(json.load(f).get("entries", []), entries)
+    table = {"generated_by": "python -m muse_bf16_proj_b200.sweep --write-table [--merge] (or --from-json of its output)",
              "device": device,
              "timing": "us = mean per launch of 30 back-to-back launches (programmatic launch), weights cold in L2",
-             "entries": table_entries(rows)}
+             "entries": entries}
     with open(TABLE_PATH, "w") as f:
         json.dump(table, f, indent=1)
     log(f"wrote {len(table['entries'])} rows to {TABLE_PATH}")

@@ -40,3 +40,13 @@ def test_committed_table_covers_reference_shapes_when_present():
                 continue
             plan, _ = d.plan(m, n, k)
             assert plan.kernel in _lib.KERNEL_NAMES
+
+
+def test_merge_replaces_only_the_swept_shapes():
+    from muse_bf16_proj_b200.sweep import merge_entries
+    old = [{"n": 10, "k": 512, "m_lo": 1, "m_hi": 4, "weights": "bf16", "plan": {"kernel": "tc_tile"}},
+           {"n": 20, "k": 512, "m_lo": 1, "m_hi": 4, "weights": "bf16", "plan": {"kernel": "tc_tile"}},
+           {"n": 20, "k": 512, "m_lo": 1, "m_hi": 2, "weights": "12b", "plan": {"kernel": "gemv_12b"}}]
+    new = [{"n": 20, "k": 512, "m_lo": 1, "m_hi": 8, "weights": "12b", "plan": {"kernel": "gemv_12t"}}]
+    got = merge_entries(old, new)
+    assert [(e["n"], e["weights"], e["plan"]["kernel"]) for e in got] == [(10, "bf16", "tc_tile"), (20, "12b", "gemv_12t")]
