@@ -1275,7 +1275,7 @@ int muse_proj_f32(const void* x, const float* w, const void* tiles, float* y, in
     if (m <= 1) e = cudaLaunchKernelEx(&cfg, muse::router_f32_kernel<1>, wf, xb, y, mi, ni, ki);
     else if (m <= 2) e = cudaLaunchKernelEx(&cfg, muse::router_f32_kernel<2>, wf, xb, y, mi, ni, ki);
     else if (m <= 4) e = cudaLaunchKernelEx(&cfg, muse::router_f32_kernel<4>, wf, xb, y, mi, ni, ki);
-    else if (m <= 8) e = cudaLaunchKernelEx(&cfg, muse::router_f32_kernel<8>, wf, xb, y, mi, ni, ki);
+    // 5..16 tokens share the 16-token instance: measured faster than an 8-token one even at M = 5.
     else if (m <= 16) e = cudaLaunchKernelEx(&cfg, muse::router_f32_kernel<16>, wf, xb, y, mi, ni, ki);
     else e = cudaLaunchKernelEx(&cfg, muse::router_f32_kernel<32>, wf, xb, y, mi, ni, ki);
     if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "router_f32 launch: %s", cudaGetErrorString(e));
