@@ -76,7 +76,7 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
             for stages in (4, 6):
                 out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=bnt, split=split, stages=stages,
                                                   flags=_lib.FLAG_GLOBAL_SPLIT)))
-        if split <= 4 and tiles * split <= sms:
+        if tiles * split <= sms:  # a cluster of `split` CTAs summing through DSMEM (all in one wave)
             out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=bnt, split=split)))
     if m >= 128:
         out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM)))
