@@ -304,6 +304,12 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
 // ---- tcgen05: TMEM allocation, UMMA, TMEM loads ---------------------------------------------
 
 // Warp-wide. Writes the allocated TMEM base address to *slot (shared memory).

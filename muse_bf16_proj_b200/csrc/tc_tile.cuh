@@ -281,32 +281,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (split > 1 && !global_split) {
     cluster_sync();  // every peer's partial is in its shared memory
     if (warp >= 2) {
-      const int rl = threadIdx.x - 64;
-      const int n = rt * 128 + rl;
-      const uint32_t mine = smem_u32(part) + static_cast<uint32_t>(rl * 4);
-      // Tokens r, r + split, ... of this tile: up to 8 at a time, each peer's 8 values in flight
-      // together, peers summed in rank order.
-      for (int j0 = static_cast<int>(rank); j0 < BNT && tt * BNT + j0 < a.M; j0 += 8 * split) {
-        float sum[8];
+      // Tokens rank, rank + split, ... of this tile. Thread = (token lane tq, row quad rq): rows
+      // 4 rq .. 4 rq + 3 as one 16-byte DSMEM load per peer; two tokens per round with every peer's
+      // loads in flight together (up to 8 peers at a time), peers summed in rank order; y stored as
+      // 4 consecutive BF16 (8 bytes) per token.
+      const int e = static_cast<int>(threadIdx.x) - 64;
+      const int tq = e >> 5, rq = e & 31;
+      const uint32_t base = smem_u32(part) + static_cast<uint32_t>(rq * 16);
+      const int ntok = (BNT - static_cast<int>(rank) + split - 1) / split;
+      const int n = rt * 128 + 4 * rq;
+      for (int u0 = 2 * tq; u0 < ntok; u0 += 8) {
+        float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+        for (int p0 = 0; p0 < split; p0 += 8) {
+          float4 v[8][2];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) sum[q] = 0.f;
-        for (int p = 0; p < split; ++p) {
-          const uint32_t peer = map_peer(mine, static_cast<uint32_t>(p));
-          float v[8];
+          for (int pp = 0; pp < 8; ++pp)
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int j = j0 + q * split;
-            v[q] = j < BNT ? ld_dsmem_f32(peer + static_cast<uint32_t>(j * 128 * 4)) : 0.f;
-          }
+            for (int t = 0; t < 2; ++t) {
+              const int p = p0 + pp, j = static_cast<int>(rank) + split * (u0 + t);
+              v[pp][t] = (p < split && u0 + t < ntok)
+                             ? ld_dsmem_v4(map_peer(base + static_cast<uint32_t>(j * 512), static_cast<uint32_t>(p)))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-          for (int q = 0; q < 8; ++q) sum[q] += v[q];
+          for (int pp = 0; pp < 8; ++pp)
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              if (p0 + pp < split) {
+                acc[t].x += v[pp][t].x;
+                acc[t].y += v[pp][t].y;
+                acc[t].z += v[pp][t].z;
+                acc[t].w += v[pp][t].w;
+              }
+            }
         }
-        if (n < a.N) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int j = j0 + q * split;
-            const int m = tt * BNT + j;
-            if (j < BNT && m < a.M) store(m, n, sum[q]);
+        for (int t = 0; t < 2; ++t) {
+          const int j = static_cast<int>(rank) + split * (u0 + t);
+          const int m = tt * BNT + j;
+          if (u0 + t >= ntok || m >= a.M) continue;
+          const float sv[4] = {acc[t].x, acc[t].y, acc[t].z, acc[t].w};
+          if (!kGather && a.y32 == nullptr && (a.N & 3) == 0 && n + 4 <= a.N) {
+            *reinterpret_cast<uint2*>(a.y + static_cast<size_t>(m) * a.N + n) =
+                make_uint2(pack_bf16x2(sv[0], sv[1]), pack_bf16x2(sv[2], sv[3]));
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (n + q < a.N) store(m, n + q, sv[q]);
           }
         }
       }
