@@ -209,14 +209,14 @@ __device__ __forceinline__ int ticket_acq_rel(int* counter) {
 }
 
 // Sum of `n` FP32 partials of 16 values each, laid out `stride` floats apart with value j at
-// +j * 128, added in index order; the loads of 4 partials at a time are in flight together.
+// +j * 128, added in index order; the loads of 6 partials at a time are in flight together.
 __device__ __forceinline__ void sum_partials16(const float* base, int n, size_t stride, float (&sum)[16]) {
 #pragma unroll
   for (int j = 0; j < 16; ++j) sum[j] = 0.f;
-  for (int p0 = 0; p0 < n; p0 += 4) {
-    float v[4][16];
+  for (int p0 = 0; p0 < n; p0 += 6) {
+    float v[6][16];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
+    for (int p = 0; p < 6; ++p) {
       if (p0 + p < n) {
         const float* src = base + static_cast<size_t>(p0 + p) * stride;
 #pragma unroll
@@ -224,7 +224,7 @@ __device__ __forceinline__ void sum_partials16(const float* base, int n, size_t 
       }
     }
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
+    for (int p = 0; p < 6; ++p) {
       if (p0 + p < n) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) sum[j] += v[p][j];
