@@ -343,6 +343,7 @@ def main():
 
     # ---- e2e through kernel_fn with host buffers --------------------------------------------
     e2e = run_e2e(state, names, layer, m, n, k, rot, K, dev, world, bytes_step, flops_step)
+    accuracy = measure_accuracy(state, names[0], weights[names[0]], xs[0], n)
 
     if fused is not None:
         fused.close()  # every rank: unmap the peers' buffers before any rank frees its own
@@ -398,6 +399,7 @@ def main():
         "gpu_launches": K,
         "clocks": clocks,
         "device_error": code,
+        "accuracy": accuracy,
     }
     if gather_out is not None:
         line["config"]["all_gather"] = ("NCCL all_gather_into_tensor of y into [P, M, N/P] plus the copy to [M, N] "
@@ -443,6 +445,23 @@ def isolated_latency_us(step, rot, stream, reps: int = 20) -> float:
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b) * 1e3)
     return statistics.median(times)
+
+
+def measure_accuracy(state, name, w, x, n) -> dict:
+    """Max-abs and relative-L2 error of one projection (this rank's shard) against a torch FP64
+    product of the same x and W on the GPU, as the reference computes its expected output
+    (reference.py:72-76, before the BF16 rounding), and the largest difference from that product
+    rounded to BF16. Runs after the timed region."""
+    import torch
+
+    from muse_bf16_proj_b200 import submission
+
+    y = submission.project(x, state, name, n).double()
+    ref = x.double() @ w[:n].double().t()
+    err = y - ref
+    return {"max_abs": float(err.abs().max()), "rel_l2": float(err.norm() / ref.norm().clamp(min=1e-300)),
+            "max_abs_vs_bf16_rounded_ref": float((y - ref.to(torch.bfloat16).double()).abs().max()),
+            "ref": "torch FP64 x . W^T on the GPU (reference.py:72-76); one step, this rank's shard"}
 
 
 def run_e2e(state, names, layer, m, n, k, rot, K, dev, world, bytes_step, flops_step):
