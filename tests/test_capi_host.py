@@ -162,3 +162,22 @@ def test_gather_argument_errors():
         _lib.ipc_export(0)
     with pytest.raises(ValueError):
         _lib.ipc_open(b"short", 0)
+
+
+def test_stream_k_scratch_sizing_and_plan_errors():
+    """Scratch sizing of the stream-K plans (12-bit GEMV, pair GEMM) and their argument checks,
+    before any device work."""
+    g12 = _lib.MusePlan(kernel=_lib.KERNEL_GEMV_12T)
+    need = _lib.scratch_bytes(1, 10240, 8192, g12)
+    assert need >= 65536 and need % 4 == 0  # tickets, then FP32 partials of shared row tiles
+    assert _lib.scratch_bytes(4, 10240, 8192, g12) > need  # partials scale with the token tile
+    with pytest.raises(_lib.MuseError) as e:  # one to four tokens
+        _lib.scratch_bytes(5, 10240, 8192, g12)
+    assert e.value.code == -3
+    with pytest.raises(_lib.MuseError) as e:  # a ring needs two stages
+        _lib.scratch_bytes(1, 10240, 8192, _lib.MusePlan(kernel=_lib.KERNEL_GEMV_12T, stages=1))
+    assert e.value.code == -7
+    sk = _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2, flags=_lib.FLAG_STREAMK)
+    need = _lib.scratch_bytes(256, 10240, 8192, sk)
+    assert need > 65536 and (need - 65536) % (2 * 128 * 256 * 4) == 0  # whole 128 KB tile halves
+    assert _lib.scratch_bytes(256, 10240, 8192, _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2)) == 0
