@@ -9,7 +9,8 @@
  * stream given (a cudaStream_t passed as void*), so they can be captured in a CUDA graph.
  *
  * Pointers named x, w, y, planes, bases, esc_* in the muse_proj_* calls are DEVICE pointers;
- * the muse_encode12 / muse_decode12 buffers are HOST pointers.
+ * the muse_encode12 / muse_decode12 buffers are HOST pointers, the muse_encode12_device* ones
+ * DEVICE pointers.
  */
 #ifndef MUSE_PROJ_H
 #define MUSE_PROJ_H
@@ -93,8 +94,8 @@ const char* muse_last_error(void);
 int muse_sm_count(int* out);
 
 /*
- * Reads the device error word that bounded waits set on timeout, writes it to *code (0 = none)
- * and clears it. Synchronizes `stream`. Returns MUSE_ERR_TIMEOUT when it was set.
+ * Reads the device error word that bounded waits set on timeout (and the device encoder on an
+ * escape outside its buffer, 0x501), writes it to *code (0 = none) and clears it. Synchronizes `stream`. Returns MUSE_ERR_TIMEOUT when it was set.
  * No counterpart in the reference (its kernels have no bounded waits).
  */
 int muse_device_error(int* code, void* stream);
@@ -317,6 +318,25 @@ int muse_encode12_sizes(int64_t n, int64_t k, int64_t* planes_bytes, int64_t* ba
  */
 int muse_encode12(const uint16_t* w, int64_t n, int64_t k, uint8_t* planes, uint8_t* bases, int32_t* esc_ptr,
                   uint32_t* esc_val, int64_t esc_cap, int64_t* n_esc, int threads);
+
+/*
+ * The same encoding on the device, step 1 of 2: from BF16 W [N, K] in device memory, writes the
+ * planes, the bases and esc_ptr (N + 1 int32: the per-row CSR offsets, esc_ptr[N] = the escape
+ * count) in exactly muse_encode12's format, into device buffers of muse_encode12_sizes' sizes.
+ * The caller reads esc_ptr[N], sizes esc_val and runs step 2. Replaces nf12_pack_cuda
+ * (submission.py:591-626), which encoded with torch ops on the GPU. K % 512 == 0, K <= 65536,
+ * N * K < 2^31; W 16-byte and planes 8-byte aligned. Launches on `stream`; no allocation.
+ */
+int muse_encode12_device(const void* w, int64_t n, int64_t k, uint8_t* planes, uint8_t* bases, int32_t* esc_ptr,
+                         void* stream);
+
+/*
+ * Step 2: the escape entries (u32 k << 16 | bits, row-major, k ascending) into esc_val, from
+ * step 1's bases and esc_ptr. An entry that would fall outside esc_val[0, esc_cap) or outside
+ * its row's range is skipped and recorded in the device error word (muse_device_error: 0x501).
+ */
+int muse_encode12_device_escapes(const void* w, int64_t n, int64_t k, const uint8_t* bases, const int32_t* esc_ptr,
+                                 uint32_t* esc_val, int64_t esc_cap, void* stream);
 
 /*
  * Host decode of the 12-bit format back to BF16 bits [N, K] (the round-trip check the reference

@@ -105,6 +105,8 @@ _SIGNATURES = {
                                      _I64, _P], _I32),
     "muse_encode12_sizes": ([_I64, _I64, ctypes.POINTER(_I64), ctypes.POINTER(_I64)], _I32),
     "muse_encode12": ([_P, _I64, _I64, _P, _P, _P, _P, _I64, ctypes.POINTER(_I64), _I32], _I32),
+    "muse_encode12_device": ([_P, _I64, _I64, _P, _P, _P, _P], _I32),
+    "muse_encode12_device_escapes": ([_P, _I64, _I64, _P, _P, _P, _I64, _P], _I32),
     "muse_decode12": ([_P, _P, _P, _P, _I64, _I64, _P, _I32], _I32),
 }
 
@@ -213,6 +215,19 @@ def tiles12_bytes(n: int, k: int) -> int:
 
 def pack_tiles12(enc: MuseEnc12, tiles12_ptr: int, stream: int) -> None:
     check(load().muse_pack_tiles12(ctypes.byref(enc), tiles12_ptr, ctypes.c_void_p(stream)))
+
+
+def encode12_device(w_ptr: int, n: int, k: int, planes_ptr: int, bases_ptr: int, esc_ptr_ptr: int,
+                    stream: int) -> None:
+    """Step 1 of the device encoder (planes, bases, esc_ptr); all device pointers."""
+    check(load().muse_encode12_device(w_ptr, n, k, planes_ptr, bases_ptr, esc_ptr_ptr, ctypes.c_void_p(stream)))
+
+
+def encode12_device_escapes(w_ptr: int, n: int, k: int, bases_ptr: int, esc_ptr_ptr: int, esc_val_ptr: int,
+                            esc_cap: int, stream: int) -> None:
+    """Step 2 of the device encoder: the escape entries into esc_val[esc_cap]."""
+    check(load().muse_encode12_device_escapes(w_ptr, n, k, bases_ptr, esc_ptr_ptr, esc_val_ptr or None, esc_cap,
+                                              ctypes.c_void_p(stream)))
 
 
 def proj_12b_tiles(enc: MuseEnc12, tiles12_ptr: int, x_ptr: int, y_ptr: int, m: int, plan: MusePlan, stream: int,

@@ -22,6 +22,7 @@
 #include "tc_skinny.cuh"
 #include "router.cuh"
 #include "gemv12t.cuh"
+#include "enc12.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -942,7 +943,8 @@ int muse_device_error(int* code, void* stream) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "device_error: %s", cudaGetErrorString(e));
   *code = static_cast<int>(v);
-  if (v) return fail(MUSE_ERR_TIMEOUT, "a kernel's bounded wait expired (device code 0x%x)", v);
+  if (v) return fail(MUSE_ERR_TIMEOUT, "device error word set (device code 0x%x: a bounded wait expired, or 0x501 an "
+                                        "escape of the device encoder outside its buffer)", v);
   return MUSE_OK;
 }
 
@@ -981,7 +983,7 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
   }
   if (weights == MUSE_WEIGHTS_12B_TILES) {
     // Stream-K over the 12-bit blocks on the tensor cores: one CTA an SM with a deep ring.
-    if (k % 512 || k > 65536) return fail(MUSE_ERR_SHAPE, "plan_default: 12-bit tiles need K % 512 == 0, K <= 65536");
+    if (k % 512 || k > 65536) return fail(MUSE_ERR_SHAPE, "plan_default: 12-bit tiles need K %% 512 == 0, K <= 65536");
     if (m <= 4) {  // few tokens: CUDA cores decode in registers (gemv12t.cuh)
       out->kernel = MUSE_KERNEL_GEMV_12T;
       out->stages = 3;
@@ -1046,7 +1048,7 @@ int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stre
   muse::clear_error();
   if (!w || !tiles) return fail(MUSE_ERR_INVALID, "pack_tiles: null pointer");
   if (n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "pack_tiles: non-positive size");
-  if (!aligned16(w) || !aligned16(tiles) || k % 8) return fail(MUSE_ERR_ALIGN, "pack_tiles: 16-byte alignment and K % 8 == 0 needed");
+  if (!aligned16(w) || !aligned16(tiles) || k % 8) return fail(MUSE_ERR_ALIGN, "pack_tiles: 16-byte alignment and K %% 8 == 0 needed");
   if (n > (int64_t(1) << 24) || k > (int64_t(1) << 24)) return fail(MUSE_ERR_SHAPE, "pack_tiles: dimension too large");
   const int nkb = static_cast<int>((k + 63) / 64);
   const long long chunks = ((n + 127) / 128) * static_cast<long long>(nkb) * 1024;
@@ -1102,7 +1104,7 @@ int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, i
   if (!x || !tiles || !y || !plan) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles: null pointer");
   if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles: non-positive size");
   if (!aligned16(x) || !aligned16(tiles) || (reinterpret_cast<uintptr_t>(y) & 1u) || (k * 2) % 16)
-    return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles: x and tiles 16-byte aligned, y 2-byte aligned, K % 8 == 0");
+    return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles: x and tiles 16-byte aligned, y 2-byte aligned, K %% 8 == 0");
   if (plan->kernel == MUSE_KERNEL_TC_STREAMK)
     return run_streamk(x, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_SKINNY)
@@ -1165,7 +1167,7 @@ int muse_tiles12_bytes(int64_t n, int64_t k, int64_t* bytes) {
   muse::clear_error();
   if (!bytes) return fail(MUSE_ERR_INVALID, "tiles12_bytes: null output");
   if (n < 1 || k < 512) return fail(MUSE_ERR_INVALID, "tiles12_bytes: need N >= 1 and K >= 512");
-  if (k % 512 || k > 65536) return fail(MUSE_ERR_SHAPE, "tiles12_bytes: need K % 512 == 0 and K <= 65536");
+  if (k % 512 || k > 65536) return fail(MUSE_ERR_SHAPE, "tiles12_bytes: need K %% 512 == 0 and K <= 65536");
   *bytes = ((n + 127) / 128) * (k / 64) * int64_t(muse::kT12Block);
   return MUSE_OK;
 }
@@ -1176,7 +1178,7 @@ int muse_pack_tiles12(const MuseEnc12* enc, void* tiles12, void* stream) {
     return fail(MUSE_ERR_INVALID, "pack_tiles12: null pointer");
   if (enc->n < 1 || enc->k < 512) return fail(MUSE_ERR_INVALID, "pack_tiles12: need N >= 1 and K >= 512");
   if (enc->k % 512 || enc->k > 65536 || enc->n > (int64_t(1) << 24))
-    return fail(MUSE_ERR_SHAPE, "pack_tiles12: need K % 512 == 0, K <= 65536 and N <= 2^24");
+    return fail(MUSE_ERR_SHAPE, "pack_tiles12: need K %% 512 == 0, K <= 65536 and N <= 2^24");
   if (!aligned16(enc->planes) || !aligned16(tiles12)) return fail(MUSE_ERR_ALIGN, "pack_tiles12: 16-byte alignment needed");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int nkb = static_cast<int>(enc->k / 64);
@@ -1191,6 +1193,47 @@ int muse_pack_tiles12(const MuseEnc12* enc, void* tiles12, void* stream) {
       enc->bases, enc->esc_ptr, enc->esc_val, static_cast<uint8_t*>(tiles12), static_cast<int>(enc->n),
       static_cast<int>(enc->k), nkb);
   return launch_error("pack_escapes12 launch");
+}
+
+// Shape and pointer checks shared by the two steps of the device encoder.
+static int check_encode12_device(const char* what, const void* w, int64_t n, int64_t k) {
+  if (!w) return fail(MUSE_ERR_INVALID, "%s: null pointer", what);
+  if (n < 1 || k < 512) return fail(MUSE_ERR_INVALID, "%s: need N >= 1 and K >= 512", what);
+  if (k % 512 || k > 65536 || n * k >= (int64_t(1) << 31))
+    return fail(MUSE_ERR_SHAPE, "%s: need K %% 512 == 0, K <= 65536 and N * K < 2^31", what);
+  if (!aligned16(w)) return fail(MUSE_ERR_ALIGN, "%s: W must be 16-byte aligned", what);
+  return MUSE_OK;
+}
+
+int muse_encode12_device(const void* w, int64_t n, int64_t k, uint8_t* planes, uint8_t* bases, int32_t* esc_ptr,
+                         void* stream) {
+  muse::clear_error();
+  if (int rc = check_encode12_device("encode12_device", w, n, k)) return rc;
+  if (!planes || !bases || !esc_ptr) return fail(MUSE_ERR_INVALID, "encode12_device: null pointer");
+  if (reinterpret_cast<uintptr_t>(planes) & 7u) return fail(MUSE_ERR_ALIGN, "encode12_device: planes must be 8-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const auto* wp = static_cast<const uint16_t*>(w);
+  const int64_t tiles = (n + muse::kEnc12Tile - 1) / muse::kEnc12Tile;  // <= 2^31 / 512 / 128: fits grid.y
+  muse::enc12_bases_kernel<<<dim3(static_cast<unsigned>(k / muse::kEnc12Tile), static_cast<unsigned>(tiles)), 128, 0,
+                             st>>>(wp, n, k, bases);
+  if (int rc = launch_error("encode12_device bases launch")) return rc;
+  const unsigned rows = static_cast<unsigned>((n + muse::kEnc12RowsPerCta - 1) / muse::kEnc12RowsPerCta);
+  muse::enc12_planes_kernel<<<rows, 32 * muse::kEnc12RowsPerCta, 0, st>>>(wp, n, k, bases, planes, esc_ptr);
+  if (int rc = launch_error("encode12_device planes launch")) return rc;
+  muse::enc12_scan_kernel<<<1, muse::kEnc12ScanThreads, 0, st>>>(esc_ptr, n);
+  return launch_error("encode12_device scan launch");
+}
+
+int muse_encode12_device_escapes(const void* w, int64_t n, int64_t k, const uint8_t* bases, const int32_t* esc_ptr,
+                                 uint32_t* esc_val, int64_t esc_cap, void* stream) {
+  muse::clear_error();
+  if (int rc = check_encode12_device("encode12_device_escapes", w, n, k)) return rc;
+  if (!bases || !esc_ptr || (esc_cap > 0 && !esc_val) || esc_cap < 0)
+    return fail(MUSE_ERR_INVALID, "encode12_device_escapes: null pointer or negative capacity");
+  const unsigned rows = static_cast<unsigned>((n + muse::kEnc12RowsPerCta - 1) / muse::kEnc12RowsPerCta);
+  muse::enc12_escapes_kernel<<<rows, 32 * muse::kEnc12RowsPerCta, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(w), n, k, bases, esc_ptr, esc_val, esc_cap);
+  return launch_error("encode12_device_escapes launch");
 }
 
 int muse_proj_12b_tiles(const MuseEnc12* enc, const void* tiles12, const void* x, void* y, int64_t m,
@@ -1215,7 +1258,7 @@ int muse_proj_bf16_tiles_f32(const void* x, const void* tiles, float* y, int64_t
   if (!x || !tiles || !y || !plan) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles_f32: null pointer");
   if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles_f32: non-positive size");
   if (!aligned16(x) || !aligned16(tiles) || (reinterpret_cast<uintptr_t>(y) & 3u) || (k * 2) % 16)
-    return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles_f32: x and tiles 16-byte aligned, y 4-byte aligned, K % 8 == 0");
+    return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles_f32: x and tiles 16-byte aligned, y 4-byte aligned, K %% 8 == 0");
   if (plan->kernel != MUSE_KERNEL_TC_TILE) return fail(MUSE_ERR_PLAN, "proj_bf16_tiles_f32: plan kernel must be TC_TILE");
   return run_tc_tile(x, nullptr, tiles, nullptr, m, n, k, *plan, scratch, scratch_bytes,
                      static_cast<cudaStream_t>(stream), y, 0);
@@ -1429,7 +1472,7 @@ extern "C" int muse_proj_bf16_tiles_noalloc(const void* x, const void* tiles, vo
   if (!x || !tiles || !y || !plan) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles_noalloc: null pointer");
   if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "proj_bf16_tiles_noalloc: non-positive size");
   if (!aligned16(x) || !aligned16(tiles) || (reinterpret_cast<uintptr_t>(y) & 1u) || (k * 2) % 16)
-    return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles_noalloc: x and tiles 16-byte aligned, y 2-byte aligned, K % 8 == 0");
+    return fail(MUSE_ERR_ALIGN, "proj_bf16_tiles_noalloc: x and tiles 16-byte aligned, y 2-byte aligned, K %% 8 == 0");
   if (plan->kernel != MUSE_KERNEL_TC_STREAMK)
     return fail(MUSE_ERR_PLAN, "proj_bf16_tiles_noalloc: plan kernel must be TC_STREAMK");
   SkShape sh;

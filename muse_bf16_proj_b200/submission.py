@@ -81,6 +81,43 @@ class _Enc12Device:
         self.tiles12 = torch.empty(_lib.tiles12_bytes(enc.n, enc.k), dtype=torch.uint8, device=device)
         _lib.pack_tiles12(self.view(enc.n), self.tiles12.data_ptr(), torch.cuda.current_stream(device).cuda_stream)
 
+    @classmethod
+    def encode_on_device(cls, w: torch.Tensor, max_escape_fraction: float = codec12.MAX_ESCAPE_FRACTION):
+        """Encodes BF16 W [N, K] on its GPU (muse_encode12_device: the host encoder's format and bits,
+        without W's trip through host memory). None when more than `max_escape_fraction` of the
+        weights escape (the escapes are then not written)."""
+        n, k = w.shape
+        dev = w.device
+        st = torch.cuda.current_stream(dev).cuda_stream
+        planes = torch.empty(codec12.plane_bytes(n, k), dtype=torch.uint8, device=dev)
+        bases = torch.empty(-(-n // codec12.TILE) * (k // codec12.TILE), dtype=torch.uint8, device=dev)
+        esc_ptr = torch.empty(n + 1, dtype=torch.int32, device=dev)
+        _lib.encode12_device(w.data_ptr(), n, k, planes.data_ptr(), bases.data_ptr(), esc_ptr.data_ptr(), st)
+        esc_ptr_host = esc_ptr.cpu().numpy()  # waits for step 1: the escape count sizes step 2
+        n_esc = int(esc_ptr_host[n])
+        if n_esc > max_escape_fraction * n * k:
+            return None
+        esc_val = torch.zeros(max(n_esc, 1), dtype=torch.int32, device=dev)
+        if n_esc:
+            _lib.encode12_device_escapes(w.data_ptr(), n, k, bases.data_ptr(), esc_ptr.data_ptr(), esc_val.data_ptr(),
+                                         n_esc, st)
+        _lib.device_error(st)  # raises if an escape fell outside its range
+        self = cls.__new__(cls)
+        self.n, self.k, self.n_esc = n, k, n_esc
+        self.planes, self.bases, self.esc_ptr, self.esc_val = planes, bases, esc_ptr, esc_val
+        self.escape_fraction = n_esc / float(n * k)
+        self._esc_ptr_host = esc_ptr_host
+        self._views = {}
+        self.tiles12 = torch.empty(_lib.tiles12_bytes(n, k), dtype=torch.uint8, device=dev)
+        _lib.pack_tiles12(self.view(n), self.tiles12.data_ptr(), st)
+        return self
+
+    def to_host(self) -> codec12.Encoded12:
+        """The encoding as host arrays (for the on-disk cache)."""
+        bases = self.bases.cpu().numpy().reshape(-(-self.n // codec12.TILE), self.k // codec12.TILE)
+        esc_val = self.esc_val[:self.n_esc].cpu().numpy().view(np.uint32).copy()
+        return codec12.Encoded12(self.planes.cpu().numpy(), bases, self._esc_ptr_host.copy(), esc_val, self.n, self.k)
+
     def view(self, n: int) -> _lib.MuseEnc12:
         v = self._views.get(n)
         if v is None:
@@ -95,13 +132,34 @@ class _Enc12Device:
                                                           self.esc_val))
 
 
+def _encode12_on_device(w: torch.Tensor, cache_dir: str | None):
+    """(_Enc12Device or None when too many weights escape, from_cache) for BF16 W on the GPU:
+    from cache_dir's file for this exact weight when there is one, else encoded on the device (and
+    written there for the next process)."""
+    path = key = None
+    if cache_dir:
+        key = codec12.weight_key(_bits(w))
+        path = os.path.join(cache_dir, f"{key}.m12")
+        enc = codec12.load(path, key)
+        if enc is not None and (enc.n, enc.k) == tuple(w.shape):
+            return _Enc12Device(enc, w.device), True
+    dev_enc = _Enc12Device.encode_on_device(w)
+    if dev_enc is not None and path is not None:
+        os.makedirs(cache_dir, exist_ok=True)
+        codec12.save(dev_enc.to_host(), path, key)
+    return dev_enc, False
+
+
 def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | None = None,
-            self_check: bool = True, verbose: bool = True, pdl: bool = True, cache_dir: str | None = None) -> dict:
+            self_check: bool = True, verbose: bool = True, pdl: bool = True, cache_dir: str | None = None,
+            encode_on_device: bool = False) -> dict:
     """Builds the state kernel_fn serves from. ``weights``: name -> W [N, K] on the GPU (BF16, or
     FP32 for the router). ``encode_12b`` forces (True) or forbids (False) the 12-bit copies; None
     lets the dispatch table decide. ``cache_dir`` (or $MUSE_12B_CACHE): where 12-bit encodings are
     kept between processes (one file per weight, keyed by the weight's hash; a stale or foreign
-    file is ignored and rewritten)."""
+    file is ignored and rewritten). ``encode_on_device``: encode on the GPU (muse_encode12_device,
+    the same bits) instead of the host encoder with its decode round trip; the known-answer
+    self-check still runs on every planned kernel."""
     _lib.load()
     disp = dispatch if dispatch is not None else Dispatch()
     state = {"weights": {}, "tiles": {}, "fp32": {}, "fp32_tiles": {}, "enc12": {}, "dispatch": disp, "checked": [],
@@ -132,6 +190,17 @@ def prepare(weights: dict, dispatch: Dispatch | None = None, encode_12b: bool | 
         widths = [n] + ([UNPOOL_SLICE] if name == "unpooler" and n > UNPOOL_SLICE else [])
         want = encode_12b if encode_12b is not None else any(disp.wants_12b(nn, k) for nn in widths)
         if want and k % codec12.UNIT == 0 and k <= 65536:
+            if encode_on_device:
+                dev_enc, cached = _encode12_on_device(w, cache_dir or os.environ.get("MUSE_12B_CACHE"))
+                if dev_enc is None or dev_enc.escape_fraction > codec12.MAX_ESCAPE_FRACTION:
+                    if verbose:
+                        print(f"muse: {name}: over {codec12.MAX_ESCAPE_FRACTION:.0%} escapes, kept BF16 only")
+                else:
+                    state["enc12"][name] = dev_enc
+                    if verbose:
+                        print(f"muse: {name}: 12-bit planes ({'cached' if cached else 'encoded on the device'}), "
+                              f"{dev_enc.n_esc} escapes ({dev_enc.escape_fraction:.4%})")
+                continue
             # From cache_dir's file for this exact weight when there is one, else encoded (raises if
             # the round trip is not bit-exact) and written there for the next process.
             enc, cached = codec12.encode_cached(_bits(w), cache_dir or os.environ.get("MUSE_12B_CACHE"))

@@ -181,3 +181,23 @@ def test_stream_k_scratch_sizing_and_plan_errors():
     need = _lib.scratch_bytes(256, 10240, 8192, sk)
     assert need > 65536 and (need - 65536) % (2 * 128 * 256 * 4) == 0  # whole 128 KB tile halves
     assert _lib.scratch_bytes(256, 10240, 8192, _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2)) == 0
+
+
+def test_device_encoder_argument_errors():
+    """muse_encode12_device / _escapes reject bad shapes, null or misaligned pointers before any launch."""
+    lib = _lib.load()
+    enc, esc = lib.muse_encode12_device, lib.muse_encode12_device_escapes
+    assert enc(None, 128, 512, 16, 16, 16, None) == -1            # null W
+    assert enc(16, 0, 512, 16, 16, 16, None) == -1                # N < 1
+    assert enc(16, 128, 256, 16, 16, 16, None) == -1              # K < 512
+    assert enc(16, 128, 1000, 16, 16, 16, None) == -3             # K % 512
+    assert enc(16, 128, 65536 + 512, 16, 16, 16, None) == -3      # K > 65536
+    assert enc(16, 1 << 20, 4096, 16, 16, 16, None) == -3         # N * K >= 2^31
+    assert b"2^31" in lib.muse_last_error()
+    assert enc(18, 128, 512, 16, 16, 16, None) == -2              # W not 16-byte aligned
+    assert enc(16, 128, 512, 12, 16, 16, None) == -2              # planes not 8-byte aligned
+    assert enc(16, 128, 512, None, 16, 16, None) == -1
+    assert esc(16, 128, 512, None, 16, 16, 8, None) == -1         # null bases
+    assert esc(16, 128, 512, 16, 16, None, 8, None) == -1         # escapes expected, no buffer
+    assert esc(16, 128, 512, 16, 16, 16, -1, None) == -1          # negative capacity
+    assert esc(16, 128, 1000, 16, 16, 16, 8, None) == -3
