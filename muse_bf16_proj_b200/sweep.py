@@ -289,7 +289,7 @@ def main():
     ap.add_argument("--ms", default=",".join(map(str, DEFAULT_MS)))
     ap.add_argument("--reps", type=int, default=40)
     ap.add_argument("--no-12b", action="store_true")
-    ap.add_argument("--out", default="gpurun_out/sweep.json")
+    ap.add_argument("--out", default="sweep.json")
     ap.add_argument("--write-table", action="store_true")
     ap.add_argument("--merge", action="store_true", help="with --write-table / --from-json: replace only the swept shapes")
     ap.add_argument("--plan", default="", help='time only this plan, e.g. {"kernel": "tc_tile", "split": 3}')

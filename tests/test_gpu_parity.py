@@ -260,7 +260,8 @@ def test_prepare_12b_kernel_fn(ref_weights):
 
 
 def test_cuda_graph_replay_with_fresh_inputs(state, ref_weights):
-    """kernel_fn captured once, replayed on new x copied into the captured input (as the judge does)."""
+    """kernel_fn captured once, replayed on new x copied into the captured input (as the reference's
+    harness runs it, validate.py:139-144)."""
     for layer, m in (("qkv_gate", 1), ("pooler", 16), ("unpooler", 256)):
         pool = [C.generate_input(m, layer, 9500 + i, device="cpu") for i in range(3)]
         data = {"x": pool[0]["x"].cuda(), "config": pool[0]["config"]}
