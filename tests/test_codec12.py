@@ -37,6 +37,33 @@ def test_all_bf16_bit_patterns_round_trip():
     assert_same(enc2, Q.encode_tiles(wb2))
 
 
+def _forced_base(c: int, perm: np.ndarray) -> np.ndarray:
+    """W [128, 1024]: the even columns hold all 65,536 BF16 patterns (shuffled by `perm`), the odd
+    columns filler weights whose E7 spreads evenly over [c, c + 7]. Per 128 x 128 tile the filler
+    (8,192 weights) outweighs the patterns (about 64 per E7 value), so every tile's base is c."""
+    rng = np.random.default_rng(c)
+    w = np.empty((128, 1024), np.uint16)
+    w[:, 0::2] = np.arange(65536, dtype=np.uint32)[perm].astype(np.uint16).reshape(128, 512)
+    e7 = c + (np.arange(128 * 512) % 8)
+    filler = (rng.integers(0, 2, 128 * 512) << 15) | (e7 << 8) | rng.integers(0, 256, 128 * 512)
+    w[:, 1::2] = filler.astype(np.uint16).reshape(128, 512)
+    return w
+
+
+def test_all_bf16_patterns_under_every_window_base():
+    """All 65,536 patterns round-trip bit for bit under each of the 121 window bases a tile can
+    take (0..120), the encoder choosing the forced base in every tile; three bases also against
+    the oracle's encoder and decoder."""
+    perm = np.random.default_rng(1).permutation(65536)
+    for c in range(121):
+        wb = _forced_base(c, perm)
+        enc = codec12.encode(wb)  # verify=True decodes and compares bit for bit
+        assert (enc.bases == c).all(), f"base {c}: got {np.unique(enc.bases)}"
+        if c in (0, 60, 120):
+            assert_same(enc, Q.encode_tiles(wb))
+            assert np.array_equal(Q.decode_tiles(enc.planes, enc.bases, enc.esc_ptr, enc.esc_val, 128, 1024), wb)
+
+
 def test_baseline_injected_weights_escape_fraction():
     w = C.generate_baseline_weight("qkv_decode", 11, device="cpu", recipe="inject")
     wb = w.view(torch.int16).numpy().view(np.uint16)

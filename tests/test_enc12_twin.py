@@ -96,3 +96,14 @@ def test_twin_short_escape_buffer_skips_and_counts(twin):
     assert skipped == enc.n_esc - cap
     assert np.array_equal(esc_val, enc.esc_val[:cap])
     assert np.array_equal(esc_ptr, enc.esc_ptr)
+
+
+def test_twin_every_window_base(twin):
+    """The device program under each of the 121 window bases (0..120), every tile forced to it by
+    filler weights, all 65,536 BF16 patterns in each matrix."""
+    from test_codec12 import _forced_base
+
+    perm = np.random.default_rng(1).permutation(65536)
+    for c in range(121):
+        enc = _same_as_host(twin, _forced_base(c, perm))
+        assert (enc.bases == c).all()
