@@ -28,7 +28,8 @@ extern "C" {
 #define MUSE_ERR_SHAPE (-3)     /* shape outside what the chosen kernel supports */
 #define MUSE_ERR_CAPACITY (-4)  /* a caller-provided buffer is too small (see the count written) */
 #define MUSE_ERR_CUDA (-5)      /* a CUDA runtime / driver call failed (message has the name) */
-#define MUSE_ERR_TIMEOUT (-6)   /* a kernel's bounded wait expired (device error word was set) */
+#define MUSE_ERR_TIMEOUT (-6)   /* the device error word was set: a kernel's bounded wait expired, or the
+                                 * device encoder skipped an escape outside its buffer (0x501) */
 #define MUSE_ERR_PLAN (-7)      /* unknown kernel id or plan field out of range */
 
 /* Kernels a plan can name. */
