@@ -169,6 +169,11 @@ class RowParallelProjection:
         if self.project_fn is not None:
             return self.project_fn(x, self.shard)
         from . import _lib
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != self.shard.shape[1]:
+            raise ValueError(f"x must be BF16 [M, {self.shard.shape[1]}] (this rank's K columns), got "
+                             f"{x.dtype} {tuple(x.shape)}")
+        if x.device != self.tiles.device:
+            raise ValueError(f"x is on {x.device}, this rank's shard on {self.tiles.device}")
         m, k = x.shape
         plan = self._plans.get(m)
         if plan is None:
@@ -320,6 +325,8 @@ class FusedGatherProjection:
             raise ValueError("tiles must be a packed shard of the same shape on the same device")
         if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != self.k or not x.is_contiguous():
             raise ValueError(f"x must be a contiguous BF16 [M, {self.k}] tensor")
+        if x.device != self.tiles.device:
+            raise ValueError(f"x is on {x.device}, this rank's shard on {self.tiles.device}")
         m = x.shape[0]
         if not 0 < m <= self.max_rows:
             raise ValueError(f"M={m} outside 1..{self.max_rows} (the y_full buffer's rows)")

@@ -311,6 +311,8 @@ def project_f32(x: torch.Tensor, state: dict, layer: str, n: int | None = None,
     n = big_n if n is None else n
     if x.dim() != 2 or x.shape[1] != k or x.dtype != torch.bfloat16 or not (0 < n <= big_n):
         raise ValueError(f"{layer}: x {tuple(x.shape)} {x.dtype}, n={n} does not match W {tuple(w.shape)}")
+    if x.device != w.device:
+        raise ValueError(f"{layer}: x is on {x.device}, W on {w.device}")
     if not x.is_contiguous():
         x = x.contiguous()
     if x.data_ptr() % 16:
@@ -337,6 +339,8 @@ def project(x: torch.Tensor, state: dict, layer: str, n: int | None = None,
     n = big_n if n is None else n
     if x.dim() != 2 or x.shape[1] != k or x.dtype != torch.bfloat16 or not (0 < n <= big_n):
         raise ValueError(f"{layer}: x {tuple(x.shape)} {x.dtype}, n={n} does not match W {tuple(w.shape)}")
+    if x.device != w.device:
+        raise ValueError(f"{layer}: x is on {x.device}, W on {w.device}")
     if not x.is_contiguous():
         x = x.contiguous()
     if x.data_ptr() % 16:
