@@ -201,3 +201,17 @@ def test_device_encoder_argument_errors():
     assert esc(16, 128, 512, 16, 16, None, 8, None) == -1         # escapes expected, no buffer
     assert esc(16, 128, 512, 16, 16, 16, -1, None) == -1          # negative capacity
     assert esc(16, 128, 1000, 16, 16, 16, 8, None) == -3
+
+
+def test_library_exports_nothing_undeclared():
+    """Every muse_* symbol the library exports is declared in include/muse_proj.h (the ABI is the
+    header, nothing beside it)."""
+    import shutil
+    import subprocess
+
+    nm = shutil.which("nm")
+    if nm is None:
+        pytest.skip("no nm")
+    out = subprocess.run([nm, "-D", "--defined-only", _lib.LIB], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.split() and line.split()[-1].startswith("muse_")}
+    assert exported == set(_lib.declared_symbols())
