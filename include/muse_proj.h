@@ -43,6 +43,9 @@ extern "C" {
 #define MUSE_KERNEL_TC_SKINNY 8  /* stream-K tcgen05 over packed tiles with W as the B operand (256 W rows an MMA) */
 #define MUSE_KERNEL_F32_GEMV 9   /* FP32 W on CUDA cores (the router), M <= 32 */
 #define MUSE_KERNEL_GEMV_12T 10  /* 12-bit tiles on CUDA cores, decoded in registers, M <= 4 */
+/* tcgen05 over row windows of the packed tiles, M <= 128: each CTA streams its own rows of W over K (no
+ * split-K fix-up), tokens as the A operand; optional K split over a cluster of 2 or 4 (DSMEM sum). */
+#define MUSE_KERNEL_TC_ROWS 11
 
 /* Plan flags. */
 #define MUSE_FLAG_GLOBAL_SPLIT 1 /* TC_TILE: reduce K-split partials through caller scratch instead of a cluster */
@@ -58,10 +61,11 @@ extern "C" {
 /* How one projection runs. Zero fields take the kernel's default. */
 typedef struct MusePlan {
   int32_t kernel; /* MUSE_KERNEL_* */
-  int32_t split;  /* TC_TILE: CTAs splitting K (cluster: 1..16; global: 1..64) */
+  int32_t split;  /* TC_TILE: CTAs splitting K (cluster: 1..16; global: 1..64); TC_ROWS: 1, 2 or 4 (cluster);
+                   * TC_GEMM2: 256-token tiles walked together as a group (0 = as many as keep 64 MB of x) */
   int32_t tile_n; /* tensor-core kernels: tokens per tile, 16/32/64/128 (TC_TILE, TC_STREAMK also 256) */
   int32_t stages; /* shared-memory ring depth (0 = kernel default) */
-  int32_t ctas;   /* GEMV, TC_STREAMK, TC_SKINNY, TC_12B: CTAs in the grid (0 = one per SM) */
+  int32_t ctas;   /* GEMV, TC_STREAMK, TC_SKINNY, TC_12B, TC_ROWS: CTAs in the grid (0 = one per SM) */
   int32_t warps;  /* GEMV: consumer warps per CTA: 4, 8 or 16 (0 = 8) */
   int32_t chunk;  /* GEMV: units per bulk copy (0 = about 16 KB) */
   int32_t flags;  /* MUSE_FLAG_* */
@@ -84,6 +88,19 @@ typedef struct MuseEnc12 {
  * No counterpart in the reference (it profiled through its judge's kernel table).
  */
 int muse_set_trace(void* records, int64_t capacity);
+
+/*
+ * Streaming-read floor: reads `bytes` of device memory at `src` into shared memory with 1-D bulk
+ * copies of `chunk` bytes (a ring of `stages` per CTA, `ctas` CTAs, 0 = one per SM; CTA c takes the
+ * c-th contiguous share) and nothing else, adding the number of chunks that landed to the device
+ * counter *count (ceil(bytes / chunk) when all did). The same copy path and grid shapes the
+ * projections stream their weights with, so its time for a projection's bytes is the floor that
+ * projection is measured against. bytes and chunk multiples of 16, src 16-byte aligned.
+ * No counterpart in the reference (it estimated W streaming with a loads-only kernel variant,
+ * qkv_tma.py:21-39).
+ */
+int muse_stream_read(const void* src, int64_t bytes, int64_t chunk, int stages, int ctas, unsigned int* count,
+                     void* stream);
 
 /* Library version string. */
 const char* muse_version(void);
@@ -156,7 +173,8 @@ int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stre
  * MUSE_KERNEL_TC_STREAMK or MUSE_KERNEL_TC_SKINNY (both always need scratch, see
  * muse_scratch_bytes; TC_SKINNY reads two tiles a k block as one 256-row B operand) or
  * MUSE_KERNEL_TC_GEMM / MUSE_KERNEL_TC_GEMM2 (prefill; replace the cuBLAS F.linear that served
- * the reference's large shapes, submission.py:1170). Each pipeline
+ * the reference's large shapes, submission.py:1170) or MUSE_KERNEL_TC_ROWS (M <= 128, no scratch;
+ * replaces nf12_gemv / wa_gemm at few tokens, submission.py:357-474, 799-890). Each pipeline
  * stage moves one contiguous 16 KB tile with a 1-D bulk copy. Replaces TmaGemm.__call__
  * (submission.py:977-988), which read its pre-swizzled W the same way, and the Triton split-K
  * bf16_gemm with its atomic tile tickets (submission.py:209-251, 1084-1107).

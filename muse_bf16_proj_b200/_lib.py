@@ -17,12 +17,12 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 MUSE_OK = 0
 ERRORS = {-1: "INVALID", -2: "ALIGN", -3: "SHAPE", -4: "CAPACITY", -5: "CUDA", -6: "TIMEOUT", -7: "PLAN"}
 KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_GEMM, KERNEL_TC_GEMM2 = 1, 2, 3, 4, 5, 6
-KERNEL_TC_12B, KERNEL_TC_SKINNY, KERNEL_F32_GEMV, KERNEL_GEMV_12T = 7, 8, 9, 10
+KERNEL_TC_12B, KERNEL_TC_SKINNY, KERNEL_F32_GEMV, KERNEL_GEMV_12T, KERNEL_TC_ROWS = 7, 8, 9, 10, 11
 KERNEL_NAMES = {KERNEL_GEMV_BF16: "gemv_bf16", KERNEL_GEMV_12B: "gemv_12b", KERNEL_TC_TILE: "tc_tile",
                 KERNEL_TC_STREAMK: "tc_streamk", KERNEL_TC_GEMM: "tc_gemm", KERNEL_TC_GEMM2: "tc_gemm2",
                 KERNEL_TC_12B: "tc_12b", KERNEL_TC_SKINNY: "tc_skinny", KERNEL_F32_GEMV: "f32_gemv",
-                KERNEL_GEMV_12T: "gemv_12t"}
-TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_SKINNY, KERNEL_TC_GEMM, KERNEL_TC_GEMM2)
+                KERNEL_GEMV_12T: "gemv_12t", KERNEL_TC_ROWS: "tc_rows"}
+TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_SKINNY, KERNEL_TC_GEMM, KERNEL_TC_GEMM2, KERNEL_TC_ROWS)
 KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
 FLAG_GLOBAL_SPLIT = 1
 FLAG_PDL = 2
@@ -108,6 +108,7 @@ _SIGNATURES = {
     "muse_encode12_device": ([_P, _I64, _I64, _P, _P, _P, _P], _I32),
     "muse_encode12_device_escapes": ([_P, _I64, _I64, _P, _P, _P, _I64, _P], _I32),
     "muse_decode12": ([_P, _P, _P, _P, _I64, _I64, _P, _I32], _I32),
+    "muse_stream_read": ([_P, _I64, _I64, _I32, _I32, _P, _P], _I32),
 }
 
 
@@ -308,3 +309,9 @@ def proj_bf16_tiles_noalloc(x_ptr: int, tiles_ptr: int, y_ptr: int, m: int, n: i
     (for callers that cannot allocate device memory); see include/muse_proj.h."""
     check(load().muse_proj_bf16_tiles_noalloc(x_ptr, tiles_ptr, y_ptr, m, n, k, ctypes.byref(plan),
                                               ctypes.c_void_p(stream)))
+
+
+def stream_read(src_ptr: int, nbytes: int, chunk: int, stages: int, ctas: int, count_ptr: int, stream: int) -> None:
+    """muse_stream_read: the bulk-copy streaming-read floor over nbytes at src_ptr; adds the chunks
+    that landed to the device u32 at count_ptr."""
+    check(load().muse_stream_read(src_ptr, nbytes, chunk, stages, ctas, count_ptr, ctypes.c_void_p(stream)))

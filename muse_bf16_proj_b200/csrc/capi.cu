@@ -23,6 +23,8 @@
 #include "router.cuh"
 #include "gemv12t.cuh"
 #include "enc12.cuh"
+#include "stream_read.cuh"
+#include "tc_rows.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -474,6 +476,124 @@ int run_streamk(const void* x, const void* tiles, void* y, int64_t m, int64_t n,
   }
 }
 
+// ---- row-window tcgen05 kernel (few tokens, no split-K fix-up) --------------------------------
+
+struct RwShape {
+  int bnt, split, groups, units16, rmax, stages;
+};
+
+int rw_shape(int64_t m, int64_t n, int64_t k, const MusePlan& p, RwShape* out) {
+  DeviceInfo* d;
+  int sms = 148, limit = kSmemLimit;
+  if (device_info(&d) == MUSE_OK) {
+    sms = d->sms;
+    limit = std::min(kSmemLimit, d->smem_optin);
+  }
+  muse::clear_error();
+  if (m > 128) return fail(MUSE_ERR_SHAPE, "tc_rows: at most 128 tokens (got %lld)", (long long)m);
+  if (n > (int64_t(1) << 24) || k > (int64_t(1) << 24)) return fail(MUSE_ERR_SHAPE, "tc_rows: dimension too large");
+  int bnt = p.tile_n;
+  if (bnt == 0) {
+    bnt = 16;
+    while (bnt < m) bnt *= 2;
+  }
+  if ((bnt != 16 && bnt != 32 && bnt != 64 && bnt != 128) || bnt < m)
+    return fail(MUSE_ERR_PLAN, "tc_rows: tile_n must be 16, 32, 64 or 128 and hold all %lld tokens (got %d)", (long long)m,
+                bnt);
+  const int nkb = static_cast<int>((k + 63) / 64);
+  const int split = p.split > 0 ? p.split : 1;
+  if ((split != 1 && split != 2 && split != 4) || split > nkb)
+    return fail(MUSE_ERR_PLAN, "tc_rows: split must be 1, 2 or 4 and at most K / 64 (got %d)", split);
+  const int units16 = static_cast<int>((n + 15) / 16);
+  int groups = (p.ctas > 0 ? p.ctas : sms) / split;
+  groups = std::max(1, std::min(groups, units16));
+  const int rmax = 16 * ((units16 + groups - 1) / groups);
+  if (rmax > muse::kRwMaxRows)
+    return fail(MUSE_ERR_PLAN, "tc_rows: %d windows leave %d rows a window (max %d): use more CTAs", groups, rmax,
+                muse::kRwMaxRows);
+  const int per = muse::rw_stage_bytes(bnt, rmax);
+  int stages = p.stages;
+  if (stages <= 0) stages = std::min(16, (limit - 1024 - 64) / (per + 16));  // the deepest ring that fits
+  if (stages < 2 || muse::rw_smem(bnt, rmax, stages) > limit)
+    return fail(MUSE_ERR_PLAN, "tc_rows: %d stages of %d bytes do not fit shared memory", stages, per);
+  if (split > 1 && static_cast<int64_t>(bnt) * rmax * 4 > static_cast<int64_t>(stages) * per)
+    return fail(MUSE_ERR_PLAN, "tc_rows: the FP32 partial does not fit the drained ring");
+  out->bnt = bnt;
+  out->split = split;
+  out->groups = groups;
+  out->units16 = units16;
+  out->rmax = rmax;
+  out->stages = stages;
+  return MUSE_OK;
+}
+
+template <int BNT>
+int launch_rw_t(const CUtensorMap& tmx, const muse::RwArgs& a, bool pdl, cudaStream_t st) {
+  auto kern = muse::tc_rows_kernel<BNT>;
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaError_t e = cudaSuccess;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_rows): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  const bool cluster = a.split > 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.groups * a.split), 1, 1);
+  cfg.blockDim = dim3(muse::kRwThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(muse::rw_smem(BNT, a.rmax, a.stages));
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(a.split);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = (pdl && !cluster) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (cluster) {
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess || clusters < 1)
+      return fail(MUSE_ERR_PLAN, "tc_rows: clusters of %d CTAs with %zu B shared memory cannot be scheduled (%s)", a.split,
+                  cfg.dynamicSmemBytes, e == cudaSuccess ? "occupancy 0" : cudaGetErrorString(e));
+  }
+  e = cudaLaunchKernelEx(&cfg, kern, tmx, a);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_rows launch (tile %d, split %d): %s", BNT, a.split, cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
+int run_rows(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p, cudaStream_t st) {
+  RwShape sh;
+  if (int rc = rw_shape(m, n, k, p, &sh)) return rc;
+  CUtensorMap tmx;
+  if (int rc = make_map(&tmx, x, m, k, sh.bnt)) return rc;
+  muse::RwArgs a;
+  a.wtiles = static_cast<const uint8_t*>(tiles);
+  a.y = static_cast<uint16_t*>(y);
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.nkb = static_cast<int>((k + 63) / 64);
+  a.stages = sh.stages;
+  a.split = sh.split;
+  a.groups = sh.groups;
+  a.units16 = sh.units16;
+  a.rmax = sh.rmax;
+  a.y_vec = (n % 8 == 0 && aligned16(y)) ? 1 : 0;
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  const bool pdl = (p.flags & MUSE_FLAG_PDL) != 0;
+  switch (sh.bnt) {
+    case 16: return launch_rw_t<16>(tmx, a, pdl, st);
+    case 32: return launch_rw_t<32>(tmx, a, pdl, st);
+    case 64: return launch_rw_t<64>(tmx, a, pdl, st);
+    default: return launch_rw_t<128>(tmx, a, pdl, st);
+  }
+}
+
 // ---- persistent prefill GEMM -------------------------------------------------------------------
 
 int run_gemm(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p,
@@ -566,6 +686,11 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   a.ntiles = static_cast<int>((n + 255) / 256);
   a.nkb = static_cast<int>((k + 63) / 64);
   a.rtiles = static_cast<int>((n + 127) / 128);
+  // Token tiles a group walks together (plan->split, else as many as keep the group's x within
+  // 64 MB, half the L2, so it stays resident while W streams past).
+  if (p.split < 0) return fail(MUSE_ERR_PLAN, "tc_gemm2: split (token tiles a group) must be >= 0");
+  a.group_m = p.split > 0 ? std::min(p.split, a.mtiles)
+                          : static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(a.mtiles, (64ll << 20) / (512 * k))));
   a.trace = g_trace.load();
   a.trace_cap = a.trace ? g_trace_cap.load() : 0;
   const long long tiles_total = static_cast<long long>(a.mtiles) * a.ntiles;
@@ -1036,6 +1161,41 @@ int muse_set_trace(void* records, int64_t capacity) {
   return MUSE_OK;
 }
 
+int muse_stream_read(const void* src, int64_t bytes, int64_t chunk, int stages, int ctas, unsigned int* count,
+                     void* stream) {
+  muse::clear_error();
+  if (!src || !count) return fail(MUSE_ERR_INVALID, "stream_read: null pointer");
+  if (bytes < 16 || chunk < 16 || bytes % 16 || chunk % 16 || chunk > (1 << 20))
+    return fail(MUSE_ERR_SHAPE, "stream_read: bytes and chunk must be positive multiples of 16 (chunk <= 1 MiB)");
+  if (!aligned16(src) || (reinterpret_cast<uintptr_t>(count) & 3u))
+    return fail(MUSE_ERR_ALIGN, "stream_read: src 16-byte and count 4-byte aligned");
+  DeviceInfo* d;
+  if (int rc = device_info(&d)) return rc;
+  if (stages < 1) return fail(MUSE_ERR_PLAN, "stream_read: stages must be positive");
+  const int smem = muse::read_floor_smem(static_cast<int>(chunk), stages);
+  if (smem > std::min(kSmemLimit, d->smem_optin))
+    return fail(MUSE_ERR_PLAN, "stream_read: %d stages of %lld bytes do not fit shared memory", stages, (long long)chunk);
+  const int64_t nch = (bytes + chunk - 1) / chunk;
+  const int grid = static_cast<int>(std::min<int64_t>(nch, ctas > 0 ? ctas : d->sms));
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  if (!configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(muse::stream_read_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(stream_read): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  muse::ReadArgs a;
+  a.src = static_cast<const uint8_t*>(src);
+  a.bytes = bytes;
+  a.chunk = static_cast<int>(chunk);
+  a.stages = stages;
+  a.count = count;
+  muse::stream_read_kernel<<<grid, 32, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  return launch_error("stream_read launch");
+}
+
 int muse_tiles_bytes(int64_t n, int64_t k, int64_t* bytes) {
   muse::clear_error();
   if (!bytes) return fail(MUSE_ERR_INVALID, "tiles_bytes: null output");
@@ -1091,6 +1251,10 @@ int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, in
     }
     return MUSE_OK;
   }
+  if (plan->kernel == MUSE_KERNEL_TC_ROWS) {  // no scratch: checks the plan only
+    RwShape rw;
+    return rw_shape(m, n, k, *plan, &rw);
+  }
   if (plan->kernel != MUSE_KERNEL_TC_TILE) return MUSE_OK;
   TcShape sh;
   if (int rc = tc_shape(m, n, k, *plan, &sh)) return rc;
@@ -1112,8 +1276,10 @@ int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, i
   if (plan->kernel == MUSE_KERNEL_TC_GEMM) return run_gemm(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_GEMM2)
     return run_gemm2(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream), nullptr, scratch, scratch_bytes);
+  if (plan->kernel == MUSE_KERNEL_TC_ROWS) return run_rows(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel != MUSE_KERNEL_TC_TILE)
-    return fail(MUSE_ERR_PLAN, "proj_bf16_tiles: plan kernel must be TC_TILE, TC_STREAMK, TC_SKINNY, TC_GEMM or TC_GEMM2");
+    return fail(MUSE_ERR_PLAN,
+                "proj_bf16_tiles: plan kernel must be TC_TILE, TC_STREAMK, TC_SKINNY, TC_GEMM, TC_GEMM2 or TC_ROWS");
   return run_tc_tile(x, nullptr, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 

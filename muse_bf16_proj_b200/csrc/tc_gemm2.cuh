@@ -11,7 +11,7 @@
 // stage is 32 KB and six fit: twice the bytes in flight of the single-CTA kernel for the same
 // UMMA work, and half of its B traffic per FLOP.
 //
-// Pairs walk the 256 x 256 tiles persistently, token tile fastest. Two TMEM accumulators
+// Pairs walk the 256 x 256 tiles persistently in groups of token tiles (g2_tile_coords). Two TMEM accumulators
 // (2 x 256 columns) overlap a tile's epilogue with the next tile's UMMAs; the odd CTA's epilogue
 // warps release an accumulator with remote arrives on the even CTA's barrier.
 #pragma once
@@ -38,6 +38,7 @@ struct G2Args {
   uint16_t* y;  // [M, N]
   int M, N, K, stages;
   int mtiles, ntiles, nkb, rtiles;  // 256-token tiles, 256-row tiles, k blocks, 128-row packed tiles
+  int group_m;  // token tiles walked together: a group's x stays in L2 while all of W streams past it
   TraceRec* trace;
   int trace_cap;
   GatherOut g;  // kGather: every value also goes to each rank's y_full (y is unused)
@@ -48,6 +49,20 @@ struct G2Args {
   float4* partials;
   int* counters;  // [tiles][2], zero between launches
 };
+
+// Tile t's coordinates in the grouped order: groups of `group_m` token tiles (the last one
+// smaller), each group walking every W tile with its token tiles fastest. A wave of the pairs then
+// covers a few W tiles times the group's token tiles, so the group's x (group_m x 256 rows) is
+// read from HBM once and stays in L2 while W streams past it, and each W tile is read once a group
+// (mtiles / group_m times in all) instead of x being re-read for every W tile.
+__device__ __forceinline__ void g2_tile_coords(const G2Args& a, int t, int& mt, int& nt) {
+  const int per_group = a.group_m * a.ntiles;
+  const int g = t / per_group, w = t - g * per_group;
+  const int m0 = g * a.group_m;
+  const int gm = min(a.group_m, a.mtiles - m0);
+  mt = m0 + w % gm;
+  nt = w / gm;
+}
 
 // The segments one pair computes, in order: whole tiles pair, pair + npairs, ... (persistent), or
 // under stream-K the pair's run of (tile, k block) units cut at tile boundaries.
@@ -137,10 +152,11 @@ __global__ void __launch_bounds__(kG2Threads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // x is re-read by every pair working on its token tile: keep it. W tiles are re-read only when
-      // there are several token tiles; with one (M <= 256) W streams through once.
+      // x is re-read by every pair working on its token tile: keep it. A W tile is read by the
+      // group's pairs at about the same time and not again until the next group: normal priority
+      // with several token tiles, evict-first with one (M <= 256: W streams through once).
       const uint64_t pol = policy_evict_last();
-      const uint64_t pol_w = a.mtiles > 1 ? pol : policy_evict_first();
+      const uint64_t pol_w = a.mtiles > 1 ? policy_evict_normal() : policy_evict_first();
       pdl_wait();
       if constexpr (kGather) gather_announce(a.g, gather_epoch(a.g));  // early, so peers rarely wait
       Ring ring;     // ring position of the next k block
@@ -149,7 +165,8 @@ __global__ void __launch_bounds__(kG2Threads, 1)
       G2Segs segs(a, pair, npairs);
       int t, kb0, kb1;
       while (ok && segs.next(t, kb0, kb1)) {
-        const int mt = t % a.mtiles, nt = t / a.mtiles;
+        int mt, nt;
+        g2_tile_coords(a, t, mt, nt);
         const int xrow = mt * 256 + static_cast<int>(rank) * 128;
         int rt = nt * 2 + static_cast<int>(rank);
         if (rt >= a.rtiles) rt = nt * 2;  // past N: a valid tile; its rows are never stored
@@ -209,7 +226,8 @@ __global__ void __launch_bounds__(kG2Threads, 1)
     int t, kb0, kb1;
     for (; segs.next(t, kb0, kb1); ++local) {
       const int b = local & 1;
-      const int mt = t % a.mtiles, nt = t / a.mtiles;
+      int mt, nt;
+      g2_tile_coords(a, t, mt, nt);
       bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], static_cast<uint32_t>((local >> 1) & 1),
                                                   kErrTcEpilogue));
       tc_fence_after();

@@ -93,7 +93,9 @@ def test_survivor_errors_instead_of_hanging(kind, how):
     assert survivor["raised"], f"rank 0's collective returned although rank 1 never joined: {survivor}"
     assert survivor["elapsed"] < BOUND_S, survivor
     msg = survivor["msg"].lower()
-    assert any(s in msg for s in ("timed out", "timeout", "closed")), survivor  # not some other error
+    # A transport error, not some other failure: gloo words a peer that left as a closed, reset or
+    # broken connection depending on which side of the socket notices first.
+    assert any(s in msg for s in ("timed out", "timeout", "closed", "reset", "broken pipe", "connection")), survivor
     if how == "never_joins":  # it waited out the process group's timeout, no longer
         assert survivor["elapsed"] >= 0.8 * PG_TIMEOUT_S, survivor
     if how == "raise":
