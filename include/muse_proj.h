@@ -46,6 +46,9 @@ extern "C" {
 /* tcgen05 over row windows of the packed tiles, M <= 128: each CTA streams its own rows of W over K (no
  * split-K fix-up), tokens as the A operand; optional K split over a cluster of 2 or 4 (DSMEM sum). */
 #define MUSE_KERNEL_TC_ROWS 11
+/* persistent tcgen05 GEMM on CTA pairs with 256 tokens x 512 W rows a tile (two N = 256 UMMAs sharing an x
+ * stage: a quarter fewer operand bytes a FLOP than TC_GEMM2); prefill with many W rows */
+#define MUSE_KERNEL_TC_WIDE 12
 
 /* Plan flags. */
 #define MUSE_FLAG_GLOBAL_SPLIT 1 /* TC_TILE: reduce K-split partials through caller scratch instead of a cluster */
@@ -62,7 +65,7 @@ extern "C" {
 typedef struct MusePlan {
   int32_t kernel; /* MUSE_KERNEL_* */
   int32_t split;  /* TC_TILE: CTAs splitting K (cluster: 1..16; global: 1..64); TC_ROWS: 1, 2 or 4 (cluster);
-                   * TC_GEMM2: 256-token tiles walked together as a group (0 = as many as keep 64 MB of x) */
+                   * TC_GEMM2, TC_WIDE: 256-token tiles walked together as a group (0 = as many as keep 32 MB of x) */
   int32_t tile_n; /* tensor-core kernels: tokens per tile, 16/32/64/128 (TC_TILE, TC_STREAMK also 256) */
   int32_t stages; /* shared-memory ring depth (0 = kernel default) */
   int32_t ctas;   /* GEMV, TC_STREAMK, TC_SKINNY, TC_12B, TC_ROWS: CTAs in the grid (0 = one per SM) */
@@ -173,7 +176,7 @@ int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stre
  * MUSE_KERNEL_TC_STREAMK or MUSE_KERNEL_TC_SKINNY (both always need scratch, see
  * muse_scratch_bytes; TC_SKINNY reads two tiles a k block as one 256-row B operand) or
  * MUSE_KERNEL_TC_GEMM / MUSE_KERNEL_TC_GEMM2 (prefill; replace the cuBLAS F.linear that served
- * the reference's large shapes, submission.py:1170) or MUSE_KERNEL_TC_ROWS (M <= 128, no scratch;
+ * the reference's large shapes, submission.py:1170; also MUSE_KERNEL_TC_WIDE) or MUSE_KERNEL_TC_ROWS (M <= 128, no scratch;
  * replaces nf12_gemv / wa_gemm at few tokens, submission.py:357-474, 799-890). Each pipeline
  * stage moves one contiguous 16 KB tile with a 1-D bulk copy. Replaces TmaGemm.__call__
  * (submission.py:977-988), which read its pre-swizzled W the same way, and the Triton split-K
@@ -181,6 +184,35 @@ int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stre
  */
 int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
                          const MusePlan* plan, void* scratch, int64_t scratch_bytes, void* stream);
+
+/* ---- window-major weights for MUSE_KERNEL_TC_ROWS ------------------------------------------------ */
+
+/* The number of row windows a TC_ROWS plan splits N into for this shape (plan->ctas, else the
+ * SM count, divided by plan->split; at most ceil(N / 16)): the `groups` of muse_pack_rows. */
+int muse_rows_groups(int64_t m, int64_t n, int64_t k, const MusePlan* plan, int* groups);
+
+/* Device bytes of the window-major copy of W [N, K]: ceil(N / 16) * 16 * ceil(K / 64) * 128. */
+int muse_rows_bytes(int64_t n, int64_t k, int groups, int64_t* bytes);
+
+/*
+ * Re-lays row-major BF16 W [N, K] (device) for `groups` row windows: the N rows are spread over the
+ * windows in 16-row units (windows differ by at most 16 rows); window g's rows for each 64-wide k
+ * block form one contiguous block, blocks in k order, in the 128-byte-swizzled order the tensor
+ * cores read (row r's 16-byte chunk c at c ^ (r % 8)); rows past N and columns past K are zero.
+ * Lossless. Device kernel on `stream`. No counterpart in the reference (its nf12 planes and wgmma
+ * tiles were laid out per kernel too, submission.py:591-626, 926-934).
+ */
+int muse_pack_rows(const void* w, void* out, int64_t n, int64_t k, int groups, void* stream);
+
+/*
+ * y = x . W^T with W as the window-major copy (muse_pack_rows with groups = muse_rows_groups for this
+ * plan and shape): each CTA streams its own rows of W over K as one sequential byte range, with no
+ * split-K fix-up. plan->kernel must be MUSE_KERNEL_TC_ROWS; M <= 128; no scratch. Replaces
+ * nf12_cuda_gemv / nf12_gemv and wa_gemm at few tokens (submission.py:660-673, 357-474, 799-890).
+ * x 16-byte aligned, K % 8 == 0.
+ */
+int muse_proj_bf16_rows(const void* x, const void* wrows, void* y, int64_t m, int64_t n, int64_t k, const MusePlan* plan,
+                        void* stream);
 
 /* ---- all-gather fused into the projection's epilogue (column-parallel shards over NVLink) ---- */
 

@@ -17,12 +17,13 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 MUSE_OK = 0
 ERRORS = {-1: "INVALID", -2: "ALIGN", -3: "SHAPE", -4: "CAPACITY", -5: "CUDA", -6: "TIMEOUT", -7: "PLAN"}
 KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_GEMM, KERNEL_TC_GEMM2 = 1, 2, 3, 4, 5, 6
-KERNEL_TC_12B, KERNEL_TC_SKINNY, KERNEL_F32_GEMV, KERNEL_GEMV_12T, KERNEL_TC_ROWS = 7, 8, 9, 10, 11
+KERNEL_TC_12B, KERNEL_TC_SKINNY, KERNEL_F32_GEMV, KERNEL_GEMV_12T, KERNEL_TC_ROWS, KERNEL_TC_WIDE = 7, 8, 9, 10, 11, 12
 KERNEL_NAMES = {KERNEL_GEMV_BF16: "gemv_bf16", KERNEL_GEMV_12B: "gemv_12b", KERNEL_TC_TILE: "tc_tile",
                 KERNEL_TC_STREAMK: "tc_streamk", KERNEL_TC_GEMM: "tc_gemm", KERNEL_TC_GEMM2: "tc_gemm2",
                 KERNEL_TC_12B: "tc_12b", KERNEL_TC_SKINNY: "tc_skinny", KERNEL_F32_GEMV: "f32_gemv",
-                KERNEL_GEMV_12T: "gemv_12t", KERNEL_TC_ROWS: "tc_rows"}
-TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_SKINNY, KERNEL_TC_GEMM, KERNEL_TC_GEMM2, KERNEL_TC_ROWS)
+                KERNEL_GEMV_12T: "gemv_12t", KERNEL_TC_ROWS: "tc_rows", KERNEL_TC_WIDE: "tc_wide"}
+TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_SKINNY, KERNEL_TC_GEMM, KERNEL_TC_GEMM2, KERNEL_TC_ROWS,
+                KERNEL_TC_WIDE)
 KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
 FLAG_GLOBAL_SPLIT = 1
 FLAG_PDL = 2
@@ -109,6 +110,10 @@ _SIGNATURES = {
     "muse_encode12_device_escapes": ([_P, _I64, _I64, _P, _P, _P, _I64, _P], _I32),
     "muse_decode12": ([_P, _P, _P, _P, _I64, _I64, _P, _I32], _I32),
     "muse_stream_read": ([_P, _I64, _I64, _I32, _I32, _P, _P], _I32),
+    "muse_rows_groups": ([_I64, _I64, _I64, ctypes.POINTER(MusePlan), ctypes.POINTER(ctypes.c_int)], _I32),
+    "muse_rows_bytes": ([_I64, _I64, _I32, ctypes.POINTER(_I64)], _I32),
+    "muse_pack_rows": ([_P, _P, _I64, _I64, _I32, _P], _I32),
+    "muse_proj_bf16_rows": ([_P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(MusePlan), _P], _I32),
 }
 
 
@@ -315,3 +320,24 @@ def stream_read(src_ptr: int, nbytes: int, chunk: int, stages: int, ctas: int, c
     """muse_stream_read: the bulk-copy streaming-read floor over nbytes at src_ptr; adds the chunks
     that landed to the device u32 at count_ptr."""
     check(load().muse_stream_read(src_ptr, nbytes, chunk, stages, ctas, count_ptr, ctypes.c_void_p(stream)))
+
+
+def rows_groups(m: int, n: int, k: int, plan: MusePlan) -> int:
+    """Row windows of a TC_ROWS plan at this shape (the groups of its window-major weight copy)."""
+    out = ctypes.c_int()
+    check(load().muse_rows_groups(m, n, k, ctypes.byref(plan), ctypes.byref(out)))
+    return out.value
+
+
+def rows_bytes(n: int, k: int, groups: int) -> int:
+    out = ctypes.c_int64()
+    check(load().muse_rows_bytes(n, k, groups, ctypes.byref(out)))
+    return out.value
+
+
+def pack_rows(w_ptr: int, out_ptr: int, n: int, k: int, groups: int, stream: int) -> None:
+    check(load().muse_pack_rows(w_ptr, out_ptr, n, k, groups, ctypes.c_void_p(stream)))
+
+
+def proj_bf16_rows(x_ptr: int, wrows_ptr: int, y_ptr: int, m: int, n: int, k: int, plan: MusePlan, stream: int) -> None:
+    check(load().muse_proj_bf16_rows(x_ptr, wrows_ptr, y_ptr, m, n, k, ctypes.byref(plan), ctypes.c_void_p(stream)))

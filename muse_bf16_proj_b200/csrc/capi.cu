@@ -25,6 +25,7 @@
 #include "enc12.cuh"
 #include "stream_read.cuh"
 #include "tc_rows.cuh"
+#include "tc_wide.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -566,13 +567,16 @@ int launch_rw_t(const CUtensorMap& tmx, const muse::RwArgs& a, bool pdl, cudaStr
   return MUSE_OK;
 }
 
-int run_rows(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p, cudaStream_t st) {
+// W as packed tiles (wrows == nullptr) or as the window-major copy (tiles == nullptr).
+int run_rows(const void* x, const void* tiles, const void* wrows, void* y, int64_t m, int64_t n, int64_t k,
+             const MusePlan& p, cudaStream_t st) {
   RwShape sh;
   if (int rc = rw_shape(m, n, k, p, &sh)) return rc;
   CUtensorMap tmx;
   if (int rc = make_map(&tmx, x, m, k, sh.bnt)) return rc;
   muse::RwArgs a;
   a.wtiles = static_cast<const uint8_t*>(tiles);
+  a.wrows = static_cast<const uint8_t*>(wrows);
   a.y = static_cast<uint16_t*>(y);
   a.M = static_cast<int>(m);
   a.N = static_cast<int>(n);
@@ -687,10 +691,11 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   a.nkb = static_cast<int>((k + 63) / 64);
   a.rtiles = static_cast<int>((n + 127) / 128);
   // Token tiles a group walks together (plan->split, else as many as keep the group's x within
-  // 64 MB, half the L2, so it stays resident while W streams past).
+  // 32 MB, a quarter of the L2, so it stays resident while W streams past; measured on a B200 at
+  // 8192 x 57344 x 8192: groups of 8 token tiles 6.17 ms, 16: 6.18-6.27 ms, all 32: 6.75 ms).
   if (p.split < 0) return fail(MUSE_ERR_PLAN, "tc_gemm2: split (token tiles a group) must be >= 0");
   a.group_m = p.split > 0 ? std::min(p.split, a.mtiles)
-                          : static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(a.mtiles, (64ll << 20) / (512 * k))));
+                          : static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(a.mtiles, (32ll << 20) / (512 * k))));
   a.trace = g_trace.load();
   a.trace_cap = a.trace ? g_trace_cap.load() : 0;
   const long long tiles_total = static_cast<long long>(a.mtiles) * a.ntiles;
@@ -755,6 +760,74 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   e = cudaLaunchKernelEx(&cfg, kern, tmx, tmw, a);
   if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_gemm2 launch: %s", cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
+// ---- wide-tile pair GEMM (256 tokens x 512 W rows a CTA pair) -------------------------------------
+
+int run_wide(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p, cudaStream_t st) {
+  DeviceInfo* d;
+  if (int rc = device_info(&d)) return rc;
+  if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "tc_wide: dimension too large");
+  const int limit = std::min(kSmemLimit, d->smem_optin);
+  const int max_stages = (limit - 1024 - 128) / (muse::kWdStage + 16);
+  const int stages = p.stages > 0 ? p.stages : max_stages;
+  if (stages < 2 || stages > max_stages) return fail(MUSE_ERR_PLAN, "tc_wide: %d stages do not fit (max %d)", stages, max_stages);
+  if (p.split < 0) return fail(MUSE_ERR_PLAN, "tc_wide: split (token tiles a group) must be >= 0");
+  muse::WdArgs a;
+  a.y = static_cast<uint16_t*>(y);
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.stages = stages;
+  a.mtiles = static_cast<int>((m + 255) / 256);
+  a.ntiles = static_cast<int>((n + 511) / 512);
+  a.nkb = static_cast<int>((k + 63) / 64);
+  a.rtiles = static_cast<int>((n + 127) / 128);
+  a.group_m = p.split > 0 ? std::min(p.split, a.mtiles)
+                          : static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(a.mtiles, (32ll << 20) / (512 * k))));
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  const long long tiles_total = static_cast<long long>(a.mtiles) * a.ntiles;
+  const long long tile_rows = static_cast<long long>(a.rtiles) * a.nkb * 128;
+  if (tiles_total > INT32_MAX || tile_rows > INT32_MAX) return fail(MUSE_ERR_SHAPE, "tc_wide: too many tiles");
+  CUtensorMap tmx, tmw;
+  if (int rc = make_map(&tmx, x, m, k, 128)) return rc;
+  // The packed tile array seen as [tiles * 128 rows, 64] BF16: a box is one 16 KB tile, copied as is.
+  if (int rc = make_map(&tmw, tiles, tile_rows, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
+  auto kern = muse::tc_wide_kernel;
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaError_t e = cudaSuccess;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_wide): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(muse::kWdThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(muse::wd_smem(stages));
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 0;  // no programmatic launch with clusters
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cfg.gridDim = dim3(2, 1, 1);
+  int clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+  if (e != cudaSuccess || clusters < 1)
+    return fail(MUSE_ERR_PLAN, "tc_wide: CTA pairs cannot be scheduled (%s)", e == cudaSuccess ? "occupancy 0" : cudaGetErrorString(e));
+  long long pairs = p.ctas > 0 ? p.ctas / 2 : clusters;
+  pairs = std::max<long long>(1, std::min<long long>({pairs, static_cast<long long>(clusters), tiles_total}));
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, tmx, tmw, a);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_wide launch: %s", cudaGetErrorString(e));
   return MUSE_OK;
 }
 
@@ -1196,6 +1269,62 @@ int muse_stream_read(const void* src, int64_t bytes, int64_t chunk, int stages, 
   return launch_error("stream_read launch");
 }
 
+static int check_rows_groups(const char* what, int64_t n, int64_t k, int groups) {
+  if (n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "%s: non-positive size", what);
+  if (n > (int64_t(1) << 24) || k > (int64_t(1) << 24)) return fail(MUSE_ERR_SHAPE, "%s: dimension too large", what);
+  const int64_t units16 = (n + 15) / 16;
+  if (groups < 1 || groups > units16)
+    return fail(MUSE_ERR_INVALID, "%s: windows must be 1 .. ceil(N / 16) = %lld (got %d)", what, (long long)units16, groups);
+  if ((units16 + groups - 1) / groups * 16 > muse::kRwMaxRows)
+    return fail(MUSE_ERR_PLAN, "%s: %d windows leave more than %d rows a window", what, groups, muse::kRwMaxRows);
+  return MUSE_OK;
+}
+
+int muse_rows_groups(int64_t m, int64_t n, int64_t k, const MusePlan* plan, int* groups) {
+  muse::clear_error();
+  if (!plan || !groups) return fail(MUSE_ERR_INVALID, "rows_groups: null pointer");
+  if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "rows_groups: non-positive size");
+  if (plan->kernel != MUSE_KERNEL_TC_ROWS) return fail(MUSE_ERR_PLAN, "rows_groups: plan kernel must be TC_ROWS");
+  RwShape sh;
+  if (int rc = rw_shape(m, n, k, *plan, &sh)) return rc;
+  *groups = sh.groups;
+  return MUSE_OK;
+}
+
+int muse_rows_bytes(int64_t n, int64_t k, int groups, int64_t* bytes) {
+  muse::clear_error();
+  if (!bytes) return fail(MUSE_ERR_INVALID, "rows_bytes: null output");
+  if (int rc = check_rows_groups("rows_bytes", n, k, groups)) return rc;
+  *bytes = ((n + 15) / 16) * 16 * ((k + 63) / 64) * 128;
+  return MUSE_OK;
+}
+
+int muse_pack_rows(const void* w, void* out, int64_t n, int64_t k, int groups, void* stream) {
+  muse::clear_error();
+  if (!w || !out) return fail(MUSE_ERR_INVALID, "pack_rows: null pointer");
+  if (int rc = check_rows_groups("pack_rows", n, k, groups)) return rc;
+  if (!aligned16(w) || !aligned16(out) || k % 8) return fail(MUSE_ERR_ALIGN, "pack_rows: 16-byte alignment and K %% 8 == 0 needed");
+  const int64_t units16 = (n + 15) / 16, nkb = (k + 63) / 64;
+  const long long chunks = static_cast<long long>(units16) * 16 * nkb * 8;
+  const int threads = 256;
+  const long long blocks = std::min<long long>((chunks + threads - 1) / threads, 148LL * 64);
+  muse::pack_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(w), static_cast<uint4*>(out), static_cast<int>(n), static_cast<int>(k),
+      static_cast<int>(nkb), static_cast<int>(units16), groups, chunks);
+  return launch_error("pack_rows launch");
+}
+
+int muse_proj_bf16_rows(const void* x, const void* wrows, void* y, int64_t m, int64_t n, int64_t k, const MusePlan* plan,
+                        void* stream) {
+  muse::clear_error();
+  if (!x || !wrows || !y || !plan) return fail(MUSE_ERR_INVALID, "proj_bf16_rows: null pointer");
+  if (m < 1 || n < 1 || k < 1) return fail(MUSE_ERR_INVALID, "proj_bf16_rows: non-positive size");
+  if (!aligned16(x) || !aligned16(wrows) || (reinterpret_cast<uintptr_t>(y) & 1u) || (k * 2) % 16)
+    return fail(MUSE_ERR_ALIGN, "proj_bf16_rows: x and wrows 16-byte aligned, y 2-byte aligned, K %% 8 == 0");
+  if (plan->kernel != MUSE_KERNEL_TC_ROWS) return fail(MUSE_ERR_PLAN, "proj_bf16_rows: plan kernel must be TC_ROWS");
+  return run_rows(x, nullptr, wrows, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
+}
+
 int muse_tiles_bytes(int64_t n, int64_t k, int64_t* bytes) {
   muse::clear_error();
   if (!bytes) return fail(MUSE_ERR_INVALID, "tiles_bytes: null output");
@@ -1276,10 +1405,12 @@ int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, i
   if (plan->kernel == MUSE_KERNEL_TC_GEMM) return run_gemm(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_GEMM2)
     return run_gemm2(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream), nullptr, scratch, scratch_bytes);
-  if (plan->kernel == MUSE_KERNEL_TC_ROWS) return run_rows(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
+  if (plan->kernel == MUSE_KERNEL_TC_ROWS)
+    return run_rows(x, tiles, nullptr, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
+  if (plan->kernel == MUSE_KERNEL_TC_WIDE) return run_wide(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel != MUSE_KERNEL_TC_TILE)
-    return fail(MUSE_ERR_PLAN,
-                "proj_bf16_tiles: plan kernel must be TC_TILE, TC_STREAMK, TC_SKINNY, TC_GEMM, TC_GEMM2 or TC_ROWS");
+    return fail(MUSE_ERR_PLAN, "proj_bf16_tiles: plan kernel must be TC_TILE, TC_STREAMK, TC_SKINNY, TC_GEMM, TC_GEMM2, "
+                               "TC_ROWS or TC_WIDE");
   return run_tc_tile(x, nullptr, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 

@@ -115,18 +115,31 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// How often a waiting thread looks at the device error word (another thread's wait gave up): every
+// kErrPollNs of waiting, on the clock. The word is one global address that every waiting warp of
+// every SM would otherwise load in its polling loop; at one load per poll the L2 slice holding it
+// saturates, and since every weight stream crosses every slice, the whole grid's streaming slowed to
+// a third (measured on a B200: 430 ns a k block instead of ~150).
+constexpr unsigned long long kErrPollNs = 20000ull;
+
 // Bounded wait for the phase of parity `parity` to complete. Returns false (after recording
-// `where`) when the limit passes, or at once when another thread already recorded an error.
+// `where`) when the limit passes, or once another thread has recorded an error (noticed within
+// kErrPollNs).
 __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, uint32_t where,
                                             unsigned long long limit_ns) {
   const unsigned long long t0 = globaltimer();
+  unsigned long long next_poll = t0 + kErrPollNs;
   for (uint32_t i = 1;; ++i) {
     if (mbar_test(bar, parity)) return true;
     if ((i & 31u) == 0u) {
-      if (error_raised()) return false;
-      if (globaltimer() - t0 > limit_ns) {
-        report_error(where);
-        return false;
+      const unsigned long long t = globaltimer();
+      if (t >= next_poll) {
+        if (error_raised()) return false;
+        if (t - t0 > limit_ns) {
+          report_error(where);
+          return false;
+        }
+        next_poll = t + kErrPollNs;
       }
     }
   }
@@ -157,12 +170,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __noinline__ bool mbar_wait_idle_slow(uint32_t bar, uint32_t parity, uint32_t where,
                                                  unsigned long long limit_ns) {
   const unsigned long long t0 = globaltimer();
+  unsigned long long next_poll = t0 + kErrPollNs;
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (error_raised()) return false;
-    if (globaltimer() - t0 > limit_ns) {
-      report_error(where);
-      return false;
+    const unsigned long long t = globaltimer();
+    if (t >= next_poll) {
+      if (error_raised()) return false;
+      if (t - t0 > limit_ns) {
+        report_error(where);
+        return false;
+      }
+      next_poll = t + kErrPollNs;
     }
   }
 }
@@ -200,11 +218,14 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 // ---- split-K tickets ---------------------------------------------------------------------------
 
 // Called by one thread after a barrier that follows every partial store of its group: publishes
-// the group's partials (release, cumulative over the barrier) and takes a ticket; returns the
-// ticket value, with acquire semantics so the reducer sees every earlier contributor's partial.
+// the group's partials and takes a ticket; returns the ticket value. The atomic's release half is
+// cumulative: the group's stores happen before it through the barrier, so they are visible to
+// whichever thread acquires the counter after it (no separate fence, which would cost a second
+// round trip to L2 on the split-K tail); its acquire half lets the reducer see every earlier
+// contributor's partial.
 __device__ __forceinline__ int ticket_acq_rel(int* counter) {
   int old;
-  asm volatile("fence.acq_rel.gpu;\n\tatom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+  asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
   return old;
 }
 

@@ -13,10 +13,17 @@
 // 48 rows already moves about 34 bytes of W a cycle through the tensor core, above an SM's share
 // of HBM bandwidth (about 23 bytes a cycle).
 //
-// W comes from the packed 16 KB tiles (muse_pack_tiles: [N/128][K/64][128 rows][64 k], each row's
-// 16-byte chunks in 128-byte-swizzle order). A window starts on a 16-row boundary, so its rows of
-// a k block are one contiguous range inside each 128-row tile it touches (one to five 1-D bulk
-// copies a k block), and the swizzle phase (row % 8) is the same in shared memory as in the tile.
+// W comes either
+//   - from the window-major copy (muse_pack_rows for the same number of windows): window g's rows
+//     for k block kb are one contiguous R x 128-byte block at 16 u0 nkb 128 + kb R 128, in the
+//     128-byte-swizzle order the UMMA reads, so a CTA streams one sequential byte range, one bulk
+//     copy a k block (the pattern HBM serves at full rate), or
+//   - from the packed 16 KB tiles (muse_pack_tiles: [N/128][K/64][128 rows][64 k]): a window's rows of
+//     a k block are a contiguous range inside each 128-row tile it touches (one to five copies a k
+//     block). Three CTAs then read slices of the same tiles at different times; measured on a
+//     B200, HBM serves that at about a third of the window-major rate (2.1 vs 6+ TB/s).
+// A window starts on a 16-row boundary, so the swizzle phase (row % 8) is the same in shared
+// memory as in either source.
 //
 // Optional K split over a thread-block cluster of `split` CTAs (2 or 4): cluster rank s takes the
 // s-th K range of the same window; after the main loop every CTA parks its FP32 partial
@@ -51,7 +58,8 @@ __host__ __device__ constexpr int rw_smem(int bnt, int rmax, int stages) {
 }
 
 struct RwArgs {
-  const uint8_t* wtiles;  // packed tiles [ceil(N/128)][nkb][16 KB]
+  const uint8_t* wtiles;  // packed tiles [ceil(N/128)][nkb][16 KB], or
+  const uint8_t* wrows;   // the window-major copy (muse_pack_rows; not null: used instead of wtiles)
   uint16_t* y;            // [M, N] BF16
   int M, N, nkb, stages, split;
   int groups;   // row windows (CTAs / split)
@@ -67,6 +75,39 @@ __host__ __device__ __forceinline__ void rw_window(int g, int groups, int units1
   const int base = units16 / groups, extra = units16 % groups;
   *u0 = g * base + (g < extra ? g : extra);
   *len = base + (g < extra ? 1 : 0);
+}
+
+// Window-major re-layout of row-major BF16 W [N, K] for `groups` windows (muse_pack_rows): window g
+// (rows 16 u0 .. 16 (u0 + len)) at byte 16 u0 nkb 128, then k block kb at + kb R 128, row r of the
+// window at + r 128 with its 16-byte chunk c (k = 64 kb + 8 c .. + 7) at position c ^ (r % 8).
+// Rows >= N and columns >= K are zero. One thread per 16-byte output chunk.
+__global__ void pack_rows_kernel(const uint16_t* __restrict__ w, uint4* __restrict__ out, int n, int k, int nkb,
+                                 int units16, int groups, long long chunks) {
+  const int base = units16 / groups, extra = units16 % groups;
+  const long long big = static_cast<long long>(extra) * (base + 1);  // units in the taller windows
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < chunks;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    // i enumerates (row, kb, c) input-side: row-major over rows, then k blocks, then chunks.
+    const int c = static_cast<int>(i & 7);
+    const long long rk = i >> 3;
+    const int kb = static_cast<int>(rk % nkb);
+    const int row = static_cast<int>(rk / nkb);
+    const int u = row >> 4;
+    int g, u0, len;
+    if (u < big) {
+      g = u / (base + 1);
+    } else {
+      g = extra + static_cast<int>((u - big) / base);
+    }
+    rw_window(g, groups, units16, &u0, &len);
+    const int r = row - 16 * u0;
+    const long long off = (static_cast<long long>(16 * u0) * nkb * 128 + static_cast<long long>(kb) * len * 16 * 128 +
+                           static_cast<long long>(r) * 128) / 16 + (c ^ (r & 7));
+    const int col = kb * 64 + c * 8;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < n && col < k) v = *reinterpret_cast<const uint4*>(w + static_cast<size_t>(row) * k + col);
+    out[off] = v;
+  }
 }
 
 template <int BNT>
@@ -106,9 +147,15 @@ __global__ void __launch_bounds__(kRwThreads, 1)
     return kb0 + (j >= nk ? j - nk : j);
   };
 
-  // The window's rows of k block kb into W stage `slot`: one bulk copy per 128-row tile touched.
+  // The window's rows of k block kb into W stage `slot`: one bulk copy of the window-major block,
+  // or one per 128-row tile touched.
+  const uint8_t* wwin = a.wrows != nullptr ? a.wrows + static_cast<size_t>(r0) * a.nkb * 128 : nullptr;
   auto load_w = [&](int kb, int slot, uint64_t pol) {
     uint8_t* dst = sw + static_cast<size_t>(slot) * sst;
+    if (wwin != nullptr) {
+      bulk_g2s(dst, wwin + static_cast<size_t>(kb) * wbytes, wbytes, &full[slot], pol);
+      return;
+    }
     for (int r = r0; r < r0 + R;) {
       const int rt = r >> 7;
       const int hi = min(r0 + R, (rt + 1) * 128);

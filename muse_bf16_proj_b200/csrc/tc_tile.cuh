@@ -117,6 +117,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int kb1 = static_cast<int>(static_cast<long long>(rank + 1) * nkb / split);
   const int nk = kb1 - kb0;
 
+  // The TMEM allocation first: a second CTA on this SM starts only once this one has allocated
+  // and relinquished its permit (measured: the second CTA an SM started ~1 us after the first when
+  // the allocation came after the barrier set-up).
+  if (warp == 1) tmem_alloc(tmem_slot, kCols);
+  const uint8_t* wsrc = a.wtiles + (static_cast<size_t>(rt) * nkb + kb0) * kTcABytes;
+  auto load_w = [&](int i, int s, uint64_t pol_w) {
+    if (tiles_mode)
+      bulk_g2s(sa + static_cast<size_t>(s) * kTcABytes, wsrc + static_cast<size_t>(i) * kTcABytes, kTcABytes, &full[s],
+               pol_w);
+    else
+      tma_load_2d(sa + static_cast<size_t>(s) * kTcABytes, &tmw, &full[s], (kb0 + i) * kTcBK, rt * 128, pol_w);
+  };
+  const int pre = min(stages, nk);
   if (threadIdx.x == 0) {
     if (!tiles_mode) prefetch_tensormap(&tmw);
     prefetch_tensormap(&tmx);
@@ -127,8 +140,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(accf, 1);
     *epi_abort = 0;
     fence_mbar_init();
+    // Weights never come from the grid this one may overlap with (programmatic launch), so the
+    // first ring-full of W streams at once, before the block barrier and the dependency wait; x
+    // only after the wait.
+    const uint64_t pol_w = policy_evict_first();
+    for (int i = 0; i < pre; ++i) {
+      mbar_expect_tx(&full[i], static_cast<uint32_t>(kTcABytes + kBBytes));
+      load_w(i, i, pol_w);
+    }
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -139,21 +159,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
-      const uint8_t* wsrc = a.wtiles + (static_cast<size_t>(rt) * nkb + kb0) * kTcABytes;
-      auto load_w = [&](int i, int s) {
-        if (tiles_mode)
-          bulk_g2s(sa + static_cast<size_t>(s) * kTcABytes, wsrc + static_cast<size_t>(i) * kTcABytes, kTcABytes,
-                   &full[s], pol_w);
-        else
-          tma_load_2d(sa + static_cast<size_t>(s) * kTcABytes, &tmw, &full[s], (kb0 + i) * kTcBK, rt * 128, pol_w);
-      };
-      // Weights never come from the grid this one may overlap with (programmatic launch), so the
-      // first ring-full of W streams before the dependency wait; x only after it.
-      const int pre = min(stages, nk);
-      for (int i = 0; i < pre; ++i) {
-        mbar_expect_tx(&full[i], static_cast<uint32_t>(kTcABytes + kBBytes));
-        load_w(i, i);
-      }
       // x's K block for W's K block kb: the same, or kb - kxb past x's end (W = [hi | lo]).
       auto xcol = [&](int kb) { return (a.kxb > 0 && kb >= a.kxb ? kb - a.kxb : kb) * kTcBK; };
       pdl_wait();
@@ -167,7 +172,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int s = ring.slot;
         if (!mbar_wait(&empty[s], ring.phase ^ 1u, kErrTcProducer)) break;
         mbar_expect_tx(&full[s], static_cast<uint32_t>(kTcABytes + kBBytes));
-        load_w(i, s);
+        load_w(i, s, pol_w);
         tma_load_2d(sb + static_cast<size_t>(s) * kBBytes, &tmx, &full[s], xcol(kb0 + i), tt * BNT, pol_x);
         ++issued;
       }

@@ -97,3 +97,57 @@ def test_rows_plan_errors():
     with pytest.raises(_lib.MuseError):
         _lib.scratch_bytes(16, 57344, 8192, rows_plan(ctas=64))  # windows of 896 rows
     assert _lib.scratch_bytes(16, 6144, 4096, rows_plan()) == 0
+
+
+def _run_rows_packed(xb, wb, plan):
+    """The window-major path: muse_pack_rows with the plan's windows, then muse_proj_bf16_rows."""
+    x, w = to_dev(xb), to_dev(wb)
+    m, k = x.shape
+    n = w.shape[0]
+    groups = _lib.rows_groups(m, n, k, plan)
+    wr = torch.empty(_lib.rows_bytes(n, k, groups), dtype=torch.uint8, device="cuda")
+    _lib.pack_rows(w.data_ptr(), wr.data_ptr(), n, k, groups, stream())
+    y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    _lib.proj_bf16_rows(x.data_ptr(), wr.data_ptr(), y.data_ptr(), m, n, k, plan, stream())
+    return y
+
+
+@pytest.mark.parametrize("n,k,m,split,ctas", CASES)
+def test_rows_window_major_parity(n, k, m, split, ctas):
+    xb, wb = _rand_bits((m, k), 31 + m + n), _rand_bits((n, k), 47 + n + k, 0.02)
+    plan = rows_plan(split=split, ctas=ctas)
+    y = _run_rows_packed(xb, wb, plan)
+    assert_parity(xb, wb, y, what=f"tc_rows window-major n={n} k={k} m={m} split={split} ctas={ctas}")
+    # The same windows and K order as the packed-tile source: bit for bit equal.
+    y2 = _run_bf16(xb, wb, plan, tiles=True)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+
+
+def test_pack_rows_layout():
+    """The window-major copy holds W's bits where the layout puts them (row r of window g, k block kb,
+    chunk c at c ^ (r % 8)); rows past N and columns past K are zero."""
+    import numpy as np
+    n, k, groups = 200, 136, 5
+    wb = _rand_bits((n, k), 9, 0.02)
+    w = to_dev(wb)
+    wr = torch.empty(_lib.rows_bytes(n, k, groups), dtype=torch.uint8, device="cuda")
+    _lib.pack_rows(w.data_ptr(), wr.data_ptr(), n, k, groups, stream())
+    torch.cuda.synchronize()
+    got = wr.cpu().numpy().view(np.uint16)
+    units16, nkb = -(-n // 16), -(-k // 64)
+    base, extra = units16 // groups, units16 % groups
+    padded = np.zeros((units16 * 16, nkb * 64), np.uint16)
+    padded[:n, :k] = wb
+    expect = np.zeros_like(got)
+    for g in range(groups):
+        u0 = g * base + min(g, extra)
+        length = base + (1 if g < extra else 0)
+        rows = 16 * length
+        for kb in range(nkb):
+            blk = (16 * u0 * nkb * 64 + kb * rows * 64)
+            for r in range(rows):
+                for c in range(8):
+                    dst = blk + r * 64 + (c ^ (r % 8)) * 8
+                    expect[dst:dst + 8] = padded[16 * u0 + r, kb * 64 + c * 8:kb * 64 + c * 8 + 8]
+    assert np.array_equal(got, expect)
