@@ -139,7 +139,8 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
  * Bytes of device scratch a plan needs (0 for most plans). Scratch holds the per-tile split-K
  * counters (first 64 KB) and FP32 partials of MUSE_FLAG_GLOBAL_SPLIT plans. The caller zeroes it
  * once; every launch leaves the counters at zero again (after a device error, zero it again).
- * Launches that share one scratch buffer must not overlap in time (use one per stream).
+ * Launches that share one scratch buffer must not overlap in time (use one per stream): they would
+ * mix their tile counters and partials.
  * No counterpart in the reference beyond its split-K counters (submission.py:112, 1126).
  */
 int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, int64_t* bytes);
@@ -251,7 +252,10 @@ int muse_ipc_close(void* ptr, int64_t offset);
  * such as reads of the previous output, is done), and the launch completes only once every
  * rank's slice is in this rank's y_full. Every wait is bounded (1 s); a rank that never joins
  * makes the others' kernels record MUSE_ERR_TIMEOUT (muse_device_error) instead of hanging.
- * All ranks must make the same sequence of calls. plan->kernel: MUSE_KERNEL_TC_TILE (decode,
+ * All ranks must make the same sequence of calls. After a call that ended with a peer timeout
+ * (device code 0x401 or 0x402), re-zero every rank's control block before the next call: a rank
+ * whose arrival wait timed out writes only its own copy and publishes no done flag, so a late peer
+ * also ends with an error rather than with a y_full missing that rank's columns. plan->kernel: MUSE_KERNEL_TC_TILE (decode,
  * small M; a K split only with MUSE_FLAG_GLOBAL_SPLIT, scratch as muse_scratch_bytes) or
  * MUSE_KERNEL_TC_GEMM2 (prefill). ldy, col0, N multiples of 8; y_full 16-byte aligned.
  * Replaces the reference's sharded serving pattern in which the unpooler slice and the MLP-up
@@ -278,7 +282,11 @@ int muse_proj_bf16_tiles_gather(const void* x, const void* tiles, int64_t m, int
  * (once per device, with that device current); make that first call before any stream capture.
  * Every call shares the one area and clears the split-K counters it uses on `stream` before its
  * launch, so calls whose execution overlaps on the GPU (other streams, other threads) race and
- * must be serialized by the caller.
+ * must be serialized by the caller. That clearing is a memset node between launches, so with a
+ * MUSE_FLAG_PDL plan this entry does not overlap its launch with the previous kernel's tail as
+ * muse_proj_bf16_tiles does. The area's device address is looked up once per device and kept for
+ * the process: after cudaDeviceReset (which unloads the library's device code) the kept address is
+ * stale, so do not call this entry again in that process after a reset.
  */
 int muse_proj_bf16_tiles_noalloc(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k,
                                  const MusePlan* plan, void* stream);

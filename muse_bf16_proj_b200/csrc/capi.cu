@@ -784,8 +784,11 @@ int run_wide(const void* x, const void* tiles, void* y, int64_t m, int64_t n, in
   a.ntiles = static_cast<int>((n + 511) / 512);
   a.nkb = static_cast<int>((k + 63) / 64);
   a.rtiles = static_cast<int>((n + 127) / 128);
+  // Token tiles a group walks together: plan->split, else as many as keep the group's x within 64 MB
+  // (measured on a B200 at 8192 x 57344 x 8192, interleaved medians: groups of 16 token tiles
+  // 6.01 ms, of 8: 6.44 ms).
   a.group_m = p.split > 0 ? std::min(p.split, a.mtiles)
-                          : static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(a.mtiles, (32ll << 20) / (512 * k))));
+                          : static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(a.mtiles, (64ll << 20) / (512 * k))));
   a.trace = g_trace.load();
   a.trace_cap = a.trace ? g_trace_cap.load() : 0;
   const long long tiles_total = static_cast<long long>(a.mtiles) * a.ntiles;
@@ -1196,7 +1199,18 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
   }
   if (m > 256) {
     if (weights != MUSE_WEIGHTS_TILES) return fail(MUSE_ERR_SHAPE, "plan_default: M > 256 needs packed tiles");
-    out->kernel = MUSE_KERNEL_TC_GEMM2;
+    // The wide-tile pair GEMM (256 x 512) moves a quarter fewer operand bytes a FLOP than the
+    // 256 x 256 one and measured about 7 % faster per tile under the power cap, but has half as many
+    // tiles: take it unless its last wave of CTA pairs leaves more of the GPU idle than that gains
+    // (measured at 8192 x {57344, 28672, 14336, 7168} x 8192 and 4096 x 10240 x 8192: the rule picks
+    // the faster kernel at each).
+    const int64_t pairs = std::max(1, sms / 2), mt = (m + 255) / 256;
+    auto wave_eff = [&](int64_t tiles) {
+      const int64_t waves = (tiles + pairs - 1) / pairs;
+      return static_cast<double>(tiles) / static_cast<double>(waves * pairs);
+    };
+    const double eff2 = wave_eff(mt * ((n + 255) / 256)), effw = wave_eff(mt * ((n + 511) / 512));
+    out->kernel = effw * 1.07 > eff2 ? MUSE_KERNEL_TC_WIDE : MUSE_KERNEL_TC_GEMM2;
     return MUSE_OK;
   }
   int bnt = 16;

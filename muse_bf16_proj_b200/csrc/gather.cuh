@@ -26,7 +26,8 @@ namespace muse {
 constexpr int kMaxPeers = 8;
 constexpr unsigned int kErrPeerArrive = 0x401, kErrPeerDone = 0x402;
 
-// One per rank, 256-byte aligned, zero-filled once when allocated.
+// One per rank, 256-byte aligned, zero-filled once when allocated (and again on every rank after any
+// call that ended with kErrPeerArrive or kErrPeerDone: a timed-out call leaves its flags behind).
 struct PeerCtl {
   unsigned int epoch;   // calls this rank has completed
   unsigned int ticket;  // CTAs of the current call that finished their stores (back to 0 after)
@@ -125,12 +126,20 @@ __device__ __forceinline__ void gather_store8(const GatherOut& g, bool peers, in
 // every ticket, makes one system-scope fence (cumulative: it covers every store ordered before the
 // tickets it observed) before it raises this rank's done flag at each peer. One system fence a
 // launch, not one a CTA. `ctas`: the grid's CTA count.
+// A call in which a wait gave up (the device error word is set: this rank's arrival wait timed
+// out, so its slice went to its own buffer only) publishes no done flag: a peer that arrives late
+// and waits for this rank's slice then ends with kErrPeerDone instead of completing with a y_full
+// that silently lacks this rank's columns.
 __device__ __forceinline__ void gather_finish(const GatherOut& g, unsigned int e, unsigned int ctas) {
   fence_acq_rel_gpu();  // release: this CTA's stores before its ticket
   PeerCtl* mine = g.ctl[g.rank];
   if (atomicAdd(&mine->ticket, 1u) != ctas - 1u) return;
   fence_acq_rel_gpu();  // acquire: every CTA's stores before what follows
   mine->ticket = 0u;  // the next call starts from 0 (it reads it only after this grid completes)
+  if (error_raised()) {
+    *reinterpret_cast<volatile unsigned int*>(&mine->epoch) = e;
+    return;
+  }
   fence_acq_rel_sys();  // release at system scope, before the done flags
   for (int p = 0; p < g.P; ++p)
     if (p != g.rank) st_relaxed_sys(&g.ctl[p]->done[g.rank], e);

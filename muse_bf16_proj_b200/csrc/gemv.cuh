@@ -13,6 +13,7 @@
 #pragma once
 
 #include "ptx.cuh"
+#include "tc12.cuh"  // decode12_bf16x8
 
 namespace muse {
 
@@ -40,27 +41,6 @@ struct GemvFormat<true> {
   static constexpr int kUnitElems = 512;
   static constexpr int kUnitBytes = 768;
 };
-
-// 8 weights from 4+4 low bytes and 8 codes (4 bytes, low nibble = even weight) with the window
-// base replicated in every byte of `base4`: out[2i], out[2i+1] = weights 2i, 2i+1 as FP32.
-// high byte = (code & 8) << 4 | (base + (code & 7)); BF16 = high << 8 | low.
-__device__ __forceinline__ void decode12_x8(uint32_t low03, uint32_t low47, uint32_t codes, uint32_t base4,
-                                            float* out) {
-  const uint32_t even = codes & 0x0F0F0F0Fu;
-  const uint32_t odd = (codes >> 4) & 0x0F0F0F0Fu;
-  const uint32_t c03 = __byte_perm(even, odd, 0x5140);  // codes of weights 0, 1, 2, 3
-  const uint32_t c47 = __byte_perm(even, odd, 0x7362);  // codes of weights 4, 5, 6, 7
-  const uint32_t h03 = ((c03 & 0x08080808u) << 4) | ((c03 & 0x07070707u) + base4);
-  const uint32_t h47 = ((c47 & 0x08080808u) << 4) | ((c47 & 0x07070707u) + base4);
-  const uint32_t p01 = __byte_perm(low03, h03, 0x5140);
-  const uint32_t p23 = __byte_perm(low03, h03, 0x7362);
-  const uint32_t p45 = __byte_perm(low47, h47, 0x5140);
-  const uint32_t p67 = __byte_perm(low47, h47, 0x7362);
-  out[0] = bf16lo(p01); out[1] = bf16hi(p01);
-  out[2] = bf16lo(p23); out[3] = bf16hi(p23);
-  out[4] = bf16lo(p45); out[5] = bf16hi(p45);
-  out[6] = bf16lo(p67); out[7] = bf16hi(p67);
-}
 
 template <int M>
 __device__ __forceinline__ void warp_sum(float (&v)[M]) {
@@ -101,9 +81,13 @@ __device__ __forceinline__ void gemv_unit(const uint8_t* ubuf, const GemvArgs& a
     const int k0 = seg * 512 + lane * 16;
     const uint32_t base = a.bases[static_cast<size_t>(row >> 7) * (a.k >> 7) + (k0 >> 7)];
     const uint32_t base4 = base * 0x01010101u;
-    float wf[16];
-    decode12_x8(lv.x, lv.y, cv.x, base4, wf);
-    decode12_x8(lv.z, lv.w, cv.y, base4, wf + 8);
+    // The window as a byte table (byte j of l03:l47 = base + j) for the table-lookup decode.
+    const uint32_t l03 = base4 + 0x03020100u, l47 = base4 + 0x07060504u;
+    const uint4 d0 = decode12_bf16x8(lv.x, lv.y, cv.x, l03, l47);
+    const uint4 d1 = decode12_bf16x8(lv.z, lv.w, cv.y, l03, l47);
+    const float wf[16] = {bf16lo(d0.x), bf16hi(d0.x), bf16lo(d0.y), bf16hi(d0.y), bf16lo(d0.z), bf16hi(d0.z),
+                          bf16lo(d0.w), bf16hi(d0.w), bf16lo(d1.x), bf16hi(d1.x), bf16lo(d1.y), bf16hi(d1.y),
+                          bf16lo(d1.z), bf16hi(d1.z), bf16lo(d1.w), bf16hi(d1.w)};
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       const uint16_t* xr = a.x + static_cast<size_t>(m) * a.k + k0;

@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(kG2Threads, 1)
       const int b = local & 1;
       int mt, nt;
       g2_tile_coords(a, t, mt, nt);
-      bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], static_cast<uint32_t>((local >> 1) & 1),
+      bool ok = __all_sync(0xffffffffu, mbar_wait_idle(&acc_full[b], static_cast<uint32_t>((local >> 1) & 1),
                                                   kErrTcEpilogue));
       tc_fence_after();
       if (a.streamk) {

@@ -78,7 +78,15 @@ class ShardedProjection:
             self._project = lambda x, out=None: submission.project(x, self.state, name, out=out)
         else:
             self.state = None
-            self._project = lambda x, out=None: project_fn(x, self.shard)
+
+            def _project(x, out=None):
+                y = project_fn(x, self.shard)
+                if out is None:
+                    return y
+                out.copy_(y)  # the caller's buffer holds the result, as on the kernel path
+                return out
+
+            self._project = _project
 
     def project(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         return self._project(x, out)

@@ -375,7 +375,14 @@ def project(x: torch.Tensor, state: dict, layer: str, n: int | None = None,
 
 
 def _scratch_for(state: dict, m: int, n: int, k: int, plan) -> torch.Tensor | None:
-    """The state's zeroed split-K scratch when the plan needs one (grown outside graph capture)."""
+    """The state's zeroed split-K scratch when the plan needs one (grown outside graph capture).
+
+    One buffer serves every layer and shape of a state: split-K plans count contributors in its
+    tile counters and park FP32 partials in it, so two projections of the same state must not run at
+    the same time on different streams (their counters and partials would mix). Calls on one stream
+    are ordered (a programmatic launch touches scratch only after its wait for the previous grid); a
+    caller that serves one state from several streams at once needs one state per stream. The
+    reference shares its split-K counters the same way (submission.py:1126)."""
     key = (m, n, k, plan.key())
     need = state["scratch_need"].get(key)
     if need is None:
@@ -393,6 +400,9 @@ def _scratch_for(state: dict, m: int, n: int, k: int, plan) -> torch.Tensor | No
 
 
 def kernel_fn(data: Inputs, state) -> torch.Tensor:
-    """data["x"] [m, k] BF16 @ W[:n].T -> [m, n] BF16 (FP32 for the router), for data["config"]["layer"]."""
+    """data["x"] [m, k] BF16 @ W[:n].T -> [m, n] BF16 (FP32 for the router), for data["config"]["layer"].
+
+    Launches on torch's current stream. One state's calls must not overlap in time on different
+    streams: they share the state's split-K scratch (see _scratch_for)."""
     cfg = data["config"]
     return project(data["x"], state, cfg["layer"], cfg["n"])

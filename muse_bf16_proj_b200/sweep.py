@@ -80,9 +80,13 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
             out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_TILE, tile_n=bnt, split=split)))
     if m >= 128:
         out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM)))
-        out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2)))
+        for group in (0, 16):  # token tiles walked together (0: as many as keep 32 MB of x)
+            out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2, split=group)))
         if m <= 2048:  # few 256 x 256 tiles: the stream-K schedule keeps every CTA pair busy
             out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2, flags=_lib.FLAG_STREAMK)))
+        if m >= 256:  # 256 x 512 pair tiles (group 0: as many as keep 64 MB of x)
+            for group in (0, 8):
+                out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_WIDE, split=group)))
     if bnt <= 128:
         for stages, ctas in ((4, 2 * sms), (6, sms), (8, sms)):
             if bnt >= 128 and ctas > sms:

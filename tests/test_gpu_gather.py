@@ -118,6 +118,33 @@ def test_peer_that_never_joins_times_out():
     assert _lib.device_error(stream) == 0
 
 
+def test_late_peer_after_a_timeout_ends_with_an_error():
+    """Two "ranks" on one GPU, run one after the other: rank 0's call times out waiting for rank 1's
+    arrival (0x401) and, having written only its own copy, publishes no done flag; rank 1 then
+    arrives late, sees rank 0's arrival, stores its slice and waits for rank 0's done flag, which
+    never comes: its call must end with 0x402, not complete as if y_full held every slice."""
+    stream = torch.cuda.current_stream().cuda_stream
+    m, n, k = 4, 1024, 2048
+    g = torch.Generator().manual_seed(7)
+    w = (torch.randn((n, k), generator=g) * 0.02).to(torch.bfloat16).cuda()
+    x = torch.randn((m, k), generator=g).to(torch.bfloat16).cuda()
+    tiles = _packed(w, stream)
+    plan = _tile_plan(16, 1)
+    y = [torch.zeros((m, 2 * n), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    ctl = torch.zeros((2, _lib.peer_ctl_bytes()), dtype=torch.uint8, device="cuda")
+    _lib.device_error(stream)  # start from a clear error word
+    for rank, expect in ((0, "0x401"), (1, "0x402")):
+        gat = _lib.MuseGather()
+        gat.world, gat.rank, gat.ldy, gat.col0 = 2, rank, 2 * n, rank * n
+        gat.y[0], gat.y[1] = y[0].data_ptr(), y[1].data_ptr()
+        gat.ctl[0], gat.ctl[1] = ctl[0].data_ptr(), ctl[1].data_ptr()
+        _lib.proj_bf16_tiles_gather(x.data_ptr(), tiles.data_ptr(), m, n, k, gat, plan, stream)
+        with pytest.raises(_lib.MuseError) as err:
+            _lib.device_error(stream)
+        assert expect in str(err.value), (rank, str(err.value))
+    assert _lib.device_error(stream) == 0
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
