@@ -8,7 +8,9 @@ each (N, K, M) every candidate plan is first checked against a torch FP32 produc
 (TF32 off; relative L2 <= 1e-3), then timed over `reps` launches with CUDA events, each launch on the next
 of R weight copies whose total exceeds the 126 MB L2 (every launch reads W cold from HBM, as the
 reference's judge flushes L2). The fastest checked plan per shape becomes a table row; 12-bit
-candidates are timed too and win a row only when faster than every BF16 plan.
+candidates are timed too and win a row only when faster than every BF16 plan. Every row also
+records cuBLAS (torch F.linear) timed the same way on the same weights: the reference's scoring
+baseline, kept as a comparator (never served).
 """
 
 from __future__ import annotations
@@ -171,6 +173,24 @@ class ShapeBench:
         return batch, statistics.mean(a.elapsed_time(b) * 1e3 for a, b in evs)
 
 
+    def cublas_us(self, m: int, reps: int) -> float:
+        """Back-to-back microseconds per call of torch's F.linear (cuBLAS) on the same rotating
+        weights and inputs: the reference's scoring baseline (baseline.py:56-60, restated as
+        F.linear in validate.py:97-105), timed as time_us times a batch. A comparator only."""
+        import torch.nn.functional as F
+        for i in range(3):
+            F.linear(self.x[i % self.rot][:m], self.w[i % self.rot])
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(int(4e6 + reps * 1e5))
+        start.record()
+        for i in range(reps):
+            F.linear(self.x[i % self.rot][:m], self.w[i % self.rot])
+        end.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) * 1e3 / reps
+
+
 def trace_plan(sb: "ShapeBench", m: int, fmt: str, plan: _lib.MusePlan, log, launches: int = 4) -> dict:
     """Runs the plan `launches` times back to back, each launch tracing into its own buffer, and
     summarises every launch on one clock: first CTA start, last CTA end, per-CTA prologue / main
@@ -239,10 +259,12 @@ def sweep_shape(n, k, ms, reps, sms, twelve, log, only=None, trace=False, extra_
                             "trace": tr})
         results.sort(key=lambda r: r["us"])
         best16 = next((r for r in results if r["fmt"] == "bf16"), None)
+        cub = sb.cublas_us(m, reps)
         for r in results[:3]:
             log(f"n={n} k={k} m={m}: {r['us']:.2f} us {r['gbs']:.0f} GB/s {r['fmt']} {r['plan']}")
+        log(f"n={n} k={k} m={m}: cuBLAS F.linear {cub:.2f} us")
         rows.append({"n": n, "k": k, "m": m, "best": results[0] if results else None, "best_bf16": best16,
-                     "all": results})
+                     "all": results, "cublas_us": cub})
     del sb
     torch.cuda.empty_cache()
     return rows
@@ -267,12 +289,17 @@ def table_entries(rows) -> list[dict]:
                     cur = None
                     continue
                 plan = {kk: v for kk, v in b["plan"].items() if v}
+                cub = r.get("cublas_us")
                 if cur is not None and cur["plan"] == plan and cur["weights"] == b["fmt"] and cur["m_hi"] == lo - 1:
                     cur["m_hi"] = hi
                     cur["us"][str(r["m"])] = round(b["us"], 3)
+                    if cub is not None:
+                        cur.setdefault("cublas_us", {})[str(r["m"])] = round(cub, 3)
                     continue
                 cur = {"n": n, "k": k, "m_lo": lo, "m_hi": hi, "weights": b["fmt"], "plan": plan,
                        "us": {str(r["m"]): round(b["us"], 3)}}
+                if cub is not None:
+                    cur["cublas_us"] = {str(r["m"]): round(cub, 3)}
                 entries.append(cur)
     entries.sort(key=lambda e: (e["n"], e["k"], 0 if e["weights"] == "12b" else 1, e["m_lo"]))
     merged = []
@@ -282,6 +309,8 @@ def table_entries(rows) -> list[dict]:
                 and p["plan"] == e["plan"] and p["m_hi"] + 1 == e["m_lo"]):
             p["m_hi"] = e["m_hi"]
             p["us"].update(e["us"])
+            if "cublas_us" in e:
+                p.setdefault("cublas_us", {}).update(e["cublas_us"])
         else:
             merged.append(e)
     return merged
@@ -358,7 +387,8 @@ def write_table(rows, device: str, log, merge: bool = False) -> None:
             entries = merge_entries(json.load(f).get("entries", []), entries)
     table = {"generated_by": "python -m muse_bf16_proj_b200.sweep --write-table [--merge] (or --from-json of its output)",
              "device": device,
-             "timing": "us = mean per launch of 30 back-to-back launches (programmatic launch), weights cold in L2",
+             "timing": ("us = mean per launch of back-to-back launches (programmatic launch), weights cold in L2; "
+                        "cublas_us = torch F.linear (cuBLAS) timed the same way on the same weights and inputs"),
              "entries": entries}
     with open(TABLE_PATH, "w") as f:
         json.dump(table, f, indent=1)

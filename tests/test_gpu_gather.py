@@ -5,8 +5,8 @@ tile-kernel call bit for bit, over repeated calls (the control block's epoch adv
 for the tile kernel (plain and K split through scratch) and the pair GEMM; and a peer that never
 joins (a second control block on the same GPU that no kernel writes) must end the launch with the
 arrival timeout in the device error word instead of a hang, this rank's own columns still written.
-On two GPUs: every rank's y_full holds every rank's columns, against the FP64 oracle and bit for
-bit against each rank's plain call. Peer pointers come from CUDA IPC handles; no TMA or bulk copy
+On 2, 4 and 8 GPUs (as many as the box has): every rank's y_full holds every rank's columns,
+against the FP64 oracle and bit for bit against each rank's plain call. Peer pointers come from CUDA IPC handles; no TMA or bulk copy
 reads a peer's memory.
 """
 
@@ -189,13 +189,14 @@ def _worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
-def test_fused_gather_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_gather_gpus(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     results = ctx.Manager().dict()
-    mp.start_processes(_worker, args=(2, _free_port(), results), nprocs=2, join=True, start_method="spawn")
-    for rank in range(2):
+    mp.start_processes(_worker, args=(world, _free_port(), results), nprocs=world, join=True, start_method="spawn")
+    for rank in range(world):
         assert results[rank], f"rank {rank} reported nothing"
         for shape, (ok, msg) in results[rank].items():
             assert ok, f"rank {rank} {shape}: {msg}"

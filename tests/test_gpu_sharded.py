@@ -1,6 +1,6 @@
-"""The sharded projections on 2 GPUs with NCCL, checked against the FP64 oracle: N-sharded (each rank
-runs the sm_100a kernels on its W shard, the all-gather rebuilds y) and K-sharded (FP32 partials,
-reduce-scatter / all-reduce). Skipped with fewer than 2 GPUs."""
+"""The sharded projections on 2, 4 and 8 GPUs with NCCL, checked against the FP64 oracle: N-sharded
+(each rank runs the sm_100a kernels on its W shard, the all-gather rebuilds y) and K-sharded (FP32
+partials, reduce-scatter / all-reduce). A world size is skipped when the box has fewer GPUs."""
 
 import os
 import socket
@@ -66,13 +66,15 @@ def _worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
-def test_sharded_projection_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_projection_gpus(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     results = manager.dict()
-    mp.start_processes(_worker, args=(2, _free_port(), results), nprocs=2, join=True, start_method="spawn")
-    for rank in range(2):
+    mp.start_processes(_worker, args=(world, _free_port(), results), nprocs=world, join=True, start_method="spawn")
+    for rank in range(world):
+        assert results[rank], f"rank {rank} reported nothing"
         for shape, (ok, msg) in results[rank].items():
             assert ok, f"rank {rank} {shape}: {msg}"
