@@ -49,6 +49,10 @@ extern "C" {
 /* persistent tcgen05 GEMM on CTA pairs with 256 tokens x 512 W rows a tile (two N = 256 UMMAs sharing an x
  * stage: a quarter fewer operand bytes a FLOP than TC_GEMM2); prefill with many W rows */
 #define MUSE_KERNEL_TC_WIDE 12
+/* tcgen05 on CTA pairs with W as the A operand: 256 W rows x tile_n tokens a pair, K split `split` ways
+ * across pairs that reduce the split together (each sums a slice of the tokens from every partial in
+ * scratch, in split order); medium M (about 32 .. 512 tokens). A split grid must fit in one wave. */
+#define MUSE_KERNEL_TC_PAIRK 13
 
 /* Plan flags. */
 #define MUSE_FLAG_GLOBAL_SPLIT 1 /* TC_TILE: reduce K-split partials through caller scratch instead of a cluster */
@@ -65,8 +69,10 @@ extern "C" {
 typedef struct MusePlan {
   int32_t kernel; /* MUSE_KERNEL_* */
   int32_t split;  /* TC_TILE: CTAs splitting K (cluster: 1..16; global: 1..64); TC_ROWS: 1, 2 or 4 (cluster);
-                   * TC_GEMM2, TC_WIDE: 256-token tiles walked together as a group (0 = as many as keep 32 MB of x) */
-  int32_t tile_n; /* tensor-core kernels: tokens per tile, 16/32/64/128 (TC_TILE, TC_STREAMK also 256) */
+                   * TC_GEMM2, TC_WIDE: 256-token tiles walked together as a group (0 = as many as keep 32 MB of x);
+                   * TC_PAIRK: CTA pairs splitting K (1..64, at most tile_n) */
+  int32_t tile_n; /* tensor-core kernels: tokens per tile, 16/32/64/128 (TC_TILE, TC_STREAMK also 256; TC_PAIRK any
+                   * multiple of 16 up to 256) */
   int32_t stages; /* shared-memory ring depth (0 = kernel default) */
   int32_t ctas;   /* GEMV, TC_STREAMK, TC_SKINNY, TC_12B, TC_ROWS: CTAs in the grid (0 = one per SM) */
   int32_t warps;  /* GEMV: consumer warps per CTA: 4, 8 or 16 (0 = 8) */
@@ -85,9 +91,10 @@ typedef struct MuseEnc12 {
 
 /*
  * Per-CTA timestamp trace for the launches that follow (debug / profiling aid; NULL turns it
- * off). `records` is a device buffer of `capacity` 48-byte records, one per CTA (CTAs past the
+ * off). `records` is a device buffer of `capacity` 64-byte records, one per CTA (CTAs past the
  * capacity are not traced): u64 globaltimer ns at kernel entry, after the prologue, after the
- * main loop, at exit; u32 SM id; u32 CTA index; 8 bytes padding. Process-wide setting.
+ * main loop, at exit; u32 SM id; u32 CTA index; six u32 kernel-specific marks (ns after the main
+ * loop; 0 where a kernel sets none). Process-wide setting.
  * No counterpart in the reference (it profiled through its judge's kernel table).
  */
 int muse_set_trace(void* records, int64_t capacity);
@@ -177,7 +184,8 @@ int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stre
  * MUSE_KERNEL_TC_STREAMK or MUSE_KERNEL_TC_SKINNY (both always need scratch, see
  * muse_scratch_bytes; TC_SKINNY reads two tiles a k block as one 256-row B operand) or
  * MUSE_KERNEL_TC_GEMM / MUSE_KERNEL_TC_GEMM2 (prefill; replace the cuBLAS F.linear that served
- * the reference's large shapes, submission.py:1170; also MUSE_KERNEL_TC_WIDE) or MUSE_KERNEL_TC_ROWS (M <= 128, no scratch;
+ * the reference's large shapes, submission.py:1170; also MUSE_KERNEL_TC_WIDE), MUSE_KERNEL_TC_PAIRK (medium M; scratch when
+ * split > 1; replaces wa_gemm's cluster split-K, submission.py:855-889) or MUSE_KERNEL_TC_ROWS (M <= 128, no scratch;
  * replaces nf12_gemv / wa_gemm at few tokens, submission.py:357-474, 799-890). Each pipeline
  * stage moves one contiguous 16 KB tile with a 1-D bulk copy. Replaces TmaGemm.__call__
  * (submission.py:977-988), which read its pre-swizzled W the same way, and the Triton split-K

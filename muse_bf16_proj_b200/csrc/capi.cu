@@ -26,6 +26,7 @@
 #include "stream_read.cuh"
 #include "tc_rows.cuh"
 #include "tc_wide.cuh"
+#include "tc_pairk.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -763,6 +764,131 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   return MUSE_OK;
 }
 
+// ---- medium-M pair GEMM (256 W rows x T tokens a CTA pair, K split reduced by the split's pairs) ----
+
+struct PkShape {
+  int t = 0, s = 1, stages = 0, nkb = 0, rtiles = 0, ttiles = 0;
+  int64_t tiles = 0, partial_bytes = 0, scratch = 0;
+};
+
+int pk_shape(int64_t m, int64_t n, int64_t k, const MusePlan& p, PkShape* out) {
+  if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "tc_pairk: dimension too large");
+  PkShape sh;
+  sh.t = p.tile_n > 0 ? p.tile_n : static_cast<int>(std::min<int64_t>(256, (m + 15) / 16 * 16));
+  if (sh.t % 16 || sh.t < 16 || sh.t > 256) return fail(MUSE_ERR_PLAN, "tc_pairk: tile_n must be a multiple of 16 in 16..256");
+  sh.nkb = static_cast<int>((k + 63) / 64);
+  sh.s = p.split > 0 ? p.split : 1;
+  if (sh.s > sh.nkb || sh.t % sh.s || sh.s > 64)
+    return fail(MUSE_ERR_PLAN, "tc_pairk: split %d must divide tile_n (%d) and not exceed the k blocks (%d) or 64", sh.s,
+                sh.t, sh.nkb);
+  sh.rtiles = static_cast<int>((n + 127) / 128);
+  sh.ttiles = static_cast<int>((m + sh.t - 1) / sh.t);
+  sh.tiles = ((n + 255) / 256) * sh.ttiles;
+  const int limit = kSmemLimit;
+  const int max_stages = (limit - 1024 - 128) / muse::pk_stage_bytes(sh.t);
+  const int per_split = (sh.nkb + sh.s - 1) / sh.s;
+  sh.stages = p.stages > 0 ? p.stages : std::max(2, std::min(max_stages, per_split));
+  if (sh.stages < 2 || muse::pk_smem(sh.t, sh.s, sh.stages) > limit)
+    return fail(MUSE_ERR_PLAN, "tc_pairk: %d stages of tile_n %d do not fit in shared memory", sh.stages, sh.t);
+  if (sh.tiles * sh.s * 2 > INT32_MAX || static_cast<int64_t>(sh.rtiles) * sh.nkb * 128 > INT32_MAX)
+    return fail(MUSE_ERR_SHAPE, "tc_pairk: too many tiles");
+  if (sh.s > 1) {
+    if (sh.tiles * 4 > kMaxCounters) return fail(MUSE_ERR_SHAPE, "tc_pairk: too many tiles for a K split");
+    sh.partial_bytes = sh.tiles * 2 * sh.s * sh.t * 128 * 4;
+    sh.scratch = kCounterBytes + sh.partial_bytes;
+  }
+  *out = sh;
+  return MUSE_OK;
+}
+
+int run_pairk(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p, void* scratch,
+              int64_t scratch_bytes, cudaStream_t st) {
+  DeviceInfo* d;
+  if (int rc = device_info(&d)) return rc;
+  PkShape sh;
+  if (int rc = pk_shape(m, n, k, p, &sh)) return rc;
+  if (sh.s > 1) {
+    if (!scratch || scratch_bytes < sh.scratch)
+      return fail(MUSE_ERR_CAPACITY, "tc_pairk: split %d needs %lld bytes of zeroed scratch (got %lld)", sh.s,
+                  (long long)sh.scratch, (long long)(scratch ? scratch_bytes : 0));
+    if (reinterpret_cast<uintptr_t>(scratch) & 255u) return fail(MUSE_ERR_ALIGN, "tc_pairk: scratch must be 256-byte aligned");
+  }
+  muse::PkArgs a;
+  a.y = static_cast<uint16_t*>(y);
+  a.partials = sh.s > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kCounterBytes) : nullptr;
+  a.counters = sh.s > 1 ? static_cast<int*>(scratch) : nullptr;
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.T = sh.t;
+  a.split = sh.s;
+  a.stages = sh.stages;
+  a.nkb = sh.nkb;
+  a.rtiles = sh.rtiles;
+  a.ttiles = sh.ttiles;
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  CUtensorMap tmx, tmw, tmy;
+  if (int rc = make_map(&tmx, x, m, k, sh.t / 2)) return rc;
+  // The packed tile array seen as [tiles * 128 rows, 64] BF16: a box is one 16 KB tile, copied as is.
+  if (int rc = make_map(&tmw, tiles, static_cast<int64_t>(sh.rtiles) * sh.nkb * 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  // y by TMA tensor stores where its rows are 16-byte multiples: boxes of 128 columns (a CTA's W rows)
+  // x T / split tokens (a reducer's slice), no swizzle.
+  a.tma_y = (n % 8 == 0 && aligned16(y)) ? 1 : 0;
+  std::memset(&tmy, 0, sizeof(tmy));
+  if (a.tma_y) {
+    auto fn = encode_fn();
+    if (!fn) return fail(MUSE_ERR_CUDA, "cuTensorMapEncodeTiled entry point not found");
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(n * 2)};
+    cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(sh.t / sh.s)};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = fn(&tmy, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MUSE_ERR_CUDA, "cuTensorMapEncodeTiled (y) failed (%d)", static_cast<int>(r));
+  }
+  auto kern = muse::tc_pairk_kernel;
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaError_t e = cudaSuccess;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_pairk): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(muse::kPkThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(muse::pk_smem(sh.t, sh.s, sh.stages));
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = (p.flags & MUSE_FLAG_PDL) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const long long pairs = sh.tiles * sh.s;
+  if (sh.s > 1) {
+    // The split's pairs wait for one another: the whole grid must be resident at once.
+    cfg.gridDim = dim3(2, 1, 1);
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess || clusters < 1)
+      return fail(MUSE_ERR_PLAN, "tc_pairk: CTA pairs cannot be scheduled (%s)", e == cudaSuccess ? "occupancy 0" : cudaGetErrorString(e));
+    if (pairs > clusters)
+      return fail(MUSE_ERR_PLAN, "tc_pairk: %lld tiles x split %d = %lld CTA pairs exceed the %d that can be resident at once",
+                  (long long)sh.tiles, sh.s, pairs, clusters);
+  }
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, tmx, tmw, tmy, a);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_pairk launch: %s", cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
 // ---- wide-tile pair GEMM (256 tokens x 512 W rows a CTA pair) -------------------------------------
 
 int run_wide(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p, cudaStream_t st) {
@@ -1394,6 +1520,12 @@ int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, in
     }
     return MUSE_OK;
   }
+  if (plan->kernel == MUSE_KERNEL_TC_PAIRK) {
+    PkShape pk;
+    if (int rc = pk_shape(m, n, k, *plan, &pk)) return rc;
+    *bytes = pk.scratch;
+    return MUSE_OK;
+  }
   if (plan->kernel == MUSE_KERNEL_TC_ROWS) {  // no scratch: checks the plan only
     RwShape rw;
     return rw_shape(m, n, k, *plan, &rw);
@@ -1422,9 +1554,11 @@ int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, i
   if (plan->kernel == MUSE_KERNEL_TC_ROWS)
     return run_rows(x, tiles, nullptr, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_WIDE) return run_wide(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
+  if (plan->kernel == MUSE_KERNEL_TC_PAIRK)
+    return run_pairk(x, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
   if (plan->kernel != MUSE_KERNEL_TC_TILE)
     return fail(MUSE_ERR_PLAN, "proj_bf16_tiles: plan kernel must be TC_TILE, TC_STREAMK, TC_SKINNY, TC_GEMM, TC_GEMM2, "
-                               "TC_ROWS or TC_WIDE");
+                               "TC_ROWS, TC_WIDE or TC_PAIRK");
   return run_tc_tile(x, nullptr, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 

@@ -52,8 +52,10 @@ __device__ __forceinline__ bool error_raised() {
 // data has been consumed, and at exit; plus the SM it ran on.
 struct TraceRec {
   unsigned long long t_start, t_ready, t_mainloop, t_end;
-  unsigned int smid, block, pad0, pad1;
+  unsigned int smid, block;
+  unsigned int x1 = 0u, x2 = 0u, x3 = 0u, x4 = 0u, x5 = 0u, x6 = 0u;  // kernel-specific marks: ns after t_mainloop
 };
+static_assert(sizeof(TraceRec) == 64, "TraceRec layout");
 
 __device__ __forceinline__ unsigned int smid() {
   unsigned int r;
@@ -296,6 +298,43 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
       : "memory");
+}
+
+// This CTA's shared memory -> global, contiguous, tracked by the issuing thread's bulk groups.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+
+// 2-D tiled tensor store from this CTA's shared memory (the map's box; the parts of the box past
+// the tensor's edges are not written). Coordinates non-negative, c0 x element size a multiple of 16.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Every bulk group this thread committed has completed (its writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Generic-proxy writes to shared memory before a later async-proxy read of them (bulk copy, UMMA).
+__device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// The same between the generic and the async proxy for global memory.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+  return v;
 }
 
 // Prefetch `bytes` (multiple of 16, 16-byte aligned) of global memory into L2, no completion signal.

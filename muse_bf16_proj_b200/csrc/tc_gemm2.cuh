@@ -368,8 +368,8 @@ __global__ void __launch_bounds__(kG2Threads, 1)
             p1.z = pack_bf16x2(v[12], v[13]);
             p1.w = pack_bf16x2(v[14], v[15]);
             uint4* dst = reinterpret_cast<uint4*>(yrow + n);
-            st_cs_v4(dst, p0);  // streaming: y must not push the group's x out of L2
-            st_cs_v4(dst + 1, p1);
+            dst[0] = p0;
+            dst[1] = p1;
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j)

@@ -220,8 +220,8 @@ __global__ void __launch_bounds__(kWdThreads, 1)
               uint4* dst = reinterpret_cast<uint4*>(yrow + n);
 #pragma unroll
               for (int j = 0; j < 4; ++j)
-                st_cs_v4(dst + j, make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
-                                             pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7])));
+                dst[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                                    pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
             } else {
 #pragma unroll
               for (int j = 0; j < 32; ++j)

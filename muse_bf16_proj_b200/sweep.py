@@ -89,6 +89,17 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
         if m >= 256:  # 256 x 512 pair tiles (group 0: as many as keep 64 MB of x)
             for group in (0, 8):
                 out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_WIDE, split=group)))
+    if 16 < m <= 1024:
+        # The pair GEMM with W as the A operand: all tokens (up to 256) or half of them a pair tile,
+        # K split across as many pairs as fill one wave (and half that).
+        pairs = sms // 2
+        rpairs = (n + 255) // 256
+        for t in sorted({min(256, (m + 15) // 16 * 16), min(256, ((m + 1) // 2 + 15) // 16 * 16)}):
+            ptiles = rpairs * ((m + t - 1) // t)
+            smax = min(pairs // ptiles, nkb, 64) if ptiles <= pairs else 1
+            divisor = lambda lim: max(d for d in range(1, max(1, lim) + 1) if t % d == 0)  # the split divides T
+            for s in sorted({divisor(smax), divisor(smax // 2)}):
+                out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_PAIRK, tile_n=t, split=s)))
     if bnt <= 128:
         for stages, ctas in ((4, 2 * sms), (6, sms), (8, sms)):
             if bnt >= 128 and ctas > sms:
@@ -211,7 +222,7 @@ def trace_plan(sb: "ShapeBench", m: int, fmt: str, plan: _lib.MusePlan, log, lau
     per, raws = [], []
     t_origin = None
     for b in bufs:
-        rec = b.cpu().numpy().reshape(cap, 6)
+        rec = b.cpu().numpy().reshape(cap, 8)
         t = rec[:, :4].astype(np.int64)
         valid = t[:, 3] > 0
         t = t[valid]
@@ -226,6 +237,11 @@ def trace_plan(sb: "ShapeBench", m: int, fmt: str, plan: _lib.MusePlan, log, lau
                     "main_max": round(float(np.max(rel[:, 2] - rel[:, 1])), 3),
                     "tail_med": round(float(np.median(rel[:, 3] - rel[:, 2])), 3),
                     "tail_max": round(float(np.max(rel[:, 3] - rel[:, 2])), 3)})
+        for c in range(6):  # kernel-specific marks: ns after the main loop's end
+            w = rec[valid, 5 + c // 2].astype(np.uint64)
+            v = (w >> np.uint64(32 * (c % 2))) & np.uint64(0xFFFFFFFF)
+            if v.any():
+                per[-1][f"mark{c + 1}_med"] = round(float(np.median(v.astype(np.float64))) / 1e3, 3)
         meta = rec[valid, 4].astype(np.uint64)
         raws.append({"t_us": rel.round(3).tolist(), "sm": (meta & 0xFFFFFFFF).astype(np.int64).tolist(),
                      "cta": ((meta >> 32) & 0xFFFFFFFF).astype(np.int64).tolist()})
@@ -234,12 +250,14 @@ def trace_plan(sb: "ShapeBench", m: int, fmt: str, plan: _lib.MusePlan, log, lau
     return {"launches": per, "raw": raws}
 
 
-def sweep_shape(n, k, ms, reps, sms, twelve, log, only=None, trace=False, extra_flags=0):
+def sweep_shape(n, k, ms, reps, sms, twelve, log, only=None, trace=False, extra_flags=0, kernels=None):
     sb = ShapeBench(n, k, max(ms), twelve)
     rows = []
     for m in ms:
         results = []
         cands = only if only is not None else candidates(m, n, k, sms, twelve and bool(sb.enc))
+        if kernels:
+            cands = [(f, p) for f, p in cands if p.as_dict()["kernel"] in kernels]
         if extra_flags:
             cands = [(f, _lib.MusePlan.from_dict({**p.as_dict(), "flags": p.flags | extra_flags})) for f, p in cands]
         for fmt, plan in cands:
@@ -328,6 +346,7 @@ def main():
     ap.add_argument("--plan", default="", help='time only this plan, e.g. {"kernel": "tc_tile", "split": 3}')
     ap.add_argument("--trace", action="store_true", help="also record per-CTA timestamps of each plan")
     ap.add_argument("--flags", type=int, default=0, help="plan flags OR-ed into every candidate (2 = PDL)")
+    ap.add_argument("--kernels", default="", help="comma-separated kernel names: time only their candidates")
     ap.add_argument("--from-json", default="", help="write the table from an earlier sweep's JSON (no GPU)")
     args = ap.parse_args()
     if args.from_json:
@@ -363,7 +382,10 @@ def main():
     rows = []
     for n, k in shapes:
         shape_ms = [m for m in ms if not (n == UNPOOL_SLICE and m > 8)]
-        rows += sweep_shape(n, k, shape_ms, args.reps, sms, not args.no_12b, log, only, args.trace, args.flags)
+        if not shape_ms:
+            continue
+        rows += sweep_shape(n, k, shape_ms, args.reps, sms, not args.no_12b, log, only, args.trace, args.flags,
+                            set(args.kernels.split(",")) if args.kernels else None)
     os.makedirs(os.path.dirname(args.out) or ".", exist_ok=True)
     with open(args.out, "w") as f:
         json.dump({"device": torch.cuda.get_device_name(), "sms": sms, "rows": rows,
