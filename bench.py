@@ -269,10 +269,12 @@ def time_b2b_us(fn, steps: int, stream) -> float:
     return a.elapsed_time(b) * 1e3 / steps
 
 
-def time_latency_us(fn, flush, reps: int = 25) -> float:
+def time_latency_us(fn, flush, reps: int = 25, stats: dict | None = None) -> float:
     """One call as the reference's judge times it (validate.py:124-147): fn captured once in a CUDA
     graph (after two warm calls on a side stream), then per rep a read of a 256 MB buffer (L2 flush)
-    and the replay between two events; the median."""
+    and the replay between two events; the median. The event clock on this part ticks in 2.048 us
+    steps, so the median moves in those steps; `stats["mean"]` (when given) is the mean over the reps,
+    which the replays' random phase against the tick resolves more finely."""
     import torch
 
     cur = torch.cuda.current_stream()
@@ -297,6 +299,8 @@ def time_latency_us(fn, flush, reps: int = 25) -> float:
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b) * 1e3)
     del g
+    if stats is not None:
+        stats["mean"] = statistics.fmean(times)
     return statistics.median(times)
 
 
@@ -416,8 +420,9 @@ def measure_comparators(wl: Workload, flush, steps: int, stream, step_us: float,
     as one call after an L2 flush; the ratios are cuBLAS time over ours (above 1: ours is faster)."""
     out = {}
     cub_step = time_b2b_us(wl.cublas_step, steps, stream)
-    cub_lat = time_latency_us(lambda: wl.cublas_step(0), flush)
-    out["cublas"] = {"step_us": round(cub_step, 3), "latency_us": round(cub_lat, 3),
+    cs = {}
+    cub_lat = time_latency_us(lambda: wl.cublas_step(0), flush, reps=60 if wl.hbm_bound else 10, stats=cs)
+    out["cublas"] = {"step_us": round(cub_step, 3), "latency_us": round(cub_lat, 3), "latency_mean_us": round(cs["mean"], 3),
                      "vs_cublas_step": round(cub_step / step_us, 4), "vs_cublas_latency": round(cub_lat / latency_us, 4),
                      "what": "torch F.linear (cuBLAS) on the BF16 weights, same rotation and timing"}
     if wl.hbm_bound:
@@ -431,17 +436,21 @@ def measure_comparators(wl: Workload, flush, steps: int, stream, step_us: float,
     return out
 
 
-def measure_config(name: str, dev, flush, stream, fixed_us: float, peaks: dict, steps: int) -> dict:
+def measure_config(name: str, dev, flush, stream, fixed_us: float, peaks: dict, steps: int,
+                   fixed_mean_us: float = 0.0) -> dict:
     """One BASELINE configuration on one GPU: back-to-back and one-call times, rate, roofline
     fraction, comparators, accuracy."""
     wl = Workload(name, dev, 1, 0)
     try:
         step_us = time_b2b_us(wl.step, steps, stream)
-        lat_us = time_latency_us(wl.call, flush)
+        ls = {}
+        lat_us = time_latency_us(wl.call, flush, reps=60 if wl.hbm_bound else 10, stats=ls)
         code = wl._lib.device_error(stream.cuda_stream)
         entry = {"m": wl.m, "n": wl.n, "k": wl.k, "weights": wl.fmt, "kernel": wl.kernel_name,
                  "plan": wl.plan.as_dict(), "step_us": round(step_us, 3), "latency_us": round(lat_us, 3),
-                 "latency_net_us": round(lat_us - fixed_us, 3), "value": round(wl.value(step_us), 4), "unit": wl.unit}
+                 "latency_net_us": round(lat_us - fixed_us, 3), "latency_mean_us": round(ls["mean"], 3),
+                 "latency_mean_net_us": round(ls["mean"] - fixed_mean_us, 3),
+                 "value": round(wl.value(step_us), 4), "unit": wl.unit}
         if wl.hbm_bound:
             entry["frac"] = round(wl.bytes_step / (step_us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)
             entry["latency_net_frac"] = round(wl.bytes_step / ((lat_us - fixed_us) * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)
@@ -534,8 +543,9 @@ def main():
 
     # ---- one call as the judge times it, the fixed replay cost, comparators ---------------------
     tiny = torch.zeros(1, device=dev)
-    fixed_us = time_latency_us(lambda: tiny.add_(1), flush, reps=40)
-    lat_us = time_latency_us(wl.call, flush, reps=25 if wl.hbm_bound else 10)
+    fs, ls = {}, {}
+    fixed_us = time_latency_us(lambda: tiny.add_(1), flush, reps=60, stats=fs)
+    lat_us = time_latency_us(wl.call, flush, reps=60 if wl.hbm_bound else 10, stats=ls)
     comps = measure_comparators(wl, flush, K, stream, step_us, lat_us)
     if world > 1:  # the slowest rank's figures
         vals = [lat_us, fixed_us, comps["cublas"]["step_us"], comps["cublas"]["latency_us"]]
@@ -589,7 +599,8 @@ def main():
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": wl.unit, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(step_us * 1e-3, 6), "step_us": round(step_us, 3),
-        "latency_us": round(lat_us, 3), "fixed_us": round(fixed_us, 3),
+        "latency_us": round(lat_us, 3), "fixed_us": round(fixed_us, 3), "latency_mean_us": round(ls["mean"], 3),
+        "fixed_mean_us": round(fs["mean"], 3),
         "latency_how": ("one kernel_fn call captured in a CUDA graph, a 256 MB read (L2 flush) then the replay between "
                         "two events, median (validate.py:139-147); fixed_us: the same for a graph of one trivial kernel"),
         "higher_is_better": True, "scaling": "strong" if wl.sharded else "weak", "vs_baseline": None,
@@ -622,7 +633,7 @@ def main():
         configs = {}
         for name in CONFIG_ORDER:
             configs[name] = head if name == HEADLINE else measure_config(name, dev, flush, stream, fixed_us, peaks,
-                                                                         max(K, 30))
+                                                                         max(K, 30), fs["mean"])
         line["configs"] = configs
     print(json.dumps(line), flush=True)
     if world > 1:

@@ -60,9 +60,11 @@ extern "C" {
  * finishes; it streams its first weights before waiting for that kernel, and touches x, y and
  * scratch only after. Only for weights that the preceding kernel in the stream does not write. */
 #define MUSE_FLAG_PDL 2
-/* TC_GEMM2: stream-K schedule. The (tile, k block) units are cut into equal runs, one per CTA
- * pair, so a grid of few 256 x 256 tiles (M = 128 .. 1024) still keeps every pair busy; tiles shared
- * by several pairs are summed from FP32 partials in scratch (muse_scratch_bytes) in a fixed order. */
+/* TC_GEMM2 and TC_PAIRK: stream-K schedule. The (tile, k block) units are cut into equal runs, one per
+ * CTA pair, so a grid of few tiles still keeps every pair busy; tiles shared by several pairs are summed
+ * from FP32 partials in scratch (muse_scratch_bytes) in a fixed order. TC_PAIRK: every pair resident at
+ * once and runs of at most one tile (the host refuses other grids); each contributor of a tile reduces
+ * a 16-token-aligned slice of it. */
 #define MUSE_FLAG_STREAMK 4
 
 /* How one projection runs. Zero fields take the kernel's default. */

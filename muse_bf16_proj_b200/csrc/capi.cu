@@ -27,6 +27,7 @@
 #include "tc_rows.cuh"
 #include "tc_wide.cuh"
 #include "tc_pairk.cuh"
+#include "tc_pairsk.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -889,6 +890,134 @@ int run_pairk(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   return MUSE_OK;
 }
 
+// Stream-K schedule of the medium-M pair GEMM (MUSE_FLAG_STREAMK on a TC_PAIRK plan).
+struct PsShape {
+  int t = 0, stages = 0, nkb = 0, rtiles = 0, ttiles = 0, cmax = 0;
+  int64_t tiles = 0, units = 0, scratch = 0;
+};
+
+// `pairs`: the CTA pairs the grid will have, at most one a unit (the scratch is sized for the most a
+// device can hold: more pairs make shorter runs and so more contributors a tile).
+int ps_shape(int64_t m, int64_t n, int64_t k, const MusePlan& p, int pairs, PsShape* out) {
+  if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "tc_pairk stream-K: dimension too large");
+  PsShape sh;
+  sh.t = p.tile_n > 0 ? p.tile_n : static_cast<int>(std::min<int64_t>(256, (m + 15) / 16 * 16));
+  if (sh.t % 16 || sh.t < 16 || sh.t > 256) return fail(MUSE_ERR_PLAN, "tc_pairk: tile_n must be a multiple of 16 in 16..256");
+  sh.nkb = static_cast<int>((k + 63) / 64);
+  sh.rtiles = static_cast<int>((n + 127) / 128);
+  sh.ttiles = static_cast<int>((m + sh.t - 1) / sh.t);
+  sh.tiles = ((n + 255) / 256) * sh.ttiles;
+  sh.units = sh.tiles * sh.nkb;
+  if (pairs < 1) return fail(MUSE_ERR_PLAN, "tc_pairk stream-K: no CTA pairs");
+  if (pairs > sh.units) pairs = static_cast<int>(sh.units);
+  if ((sh.units + pairs - 1) / pairs > sh.nkb)
+    return fail(MUSE_ERR_PLAN, "tc_pairk stream-K: runs of %lld k blocks exceed a tile's %d (more tiles than pairs can share: "
+                               "use the split or the prefill kernels)", (long long)((sh.units + pairs - 1) / pairs), sh.nkb);
+  const int max_stages = (kSmemLimit - 1024 - 128) / muse::pk_stage_bytes(sh.t);
+  sh.stages = p.stages > 0 ? p.stages : max_stages;
+  if (sh.stages < 2 || muse::ps_smem(sh.t, sh.stages) > kSmemLimit)
+    return fail(MUSE_ERR_PLAN, "tc_pairk stream-K: %d stages of tile_n %d do not fit in shared memory", sh.stages, sh.t);
+  if (sh.tiles * 4 > kMaxCounters) return fail(MUSE_ERR_SHAPE, "tc_pairk stream-K: too many tiles");
+  int cmax = 1;
+  for (int64_t t = 0; t < sh.tiles; ++t) {
+    const int first = muse::t12_owner(t * sh.nkb, sh.units, pairs), last = muse::t12_owner((t + 1) * sh.nkb - 1, sh.units, pairs);
+    cmax = std::max(cmax, last - first + 1);
+  }
+  sh.cmax = cmax;
+  sh.scratch = kCounterBytes + sh.tiles * 2 * cmax * sh.t * 128 * 4;
+  *out = sh;
+  return MUSE_OK;
+}
+
+int run_pairsk(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p, void* scratch,
+               int64_t scratch_bytes, cudaStream_t st) {
+  DeviceInfo* d;
+  if (int rc = device_info(&d)) return rc;
+  auto kern = muse::tc_pairsk_kernel;
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaError_t e = cudaSuccess;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(tc_pairsk): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  // The scratch bound: contributors a tile with every pair the device has.
+  PsShape bound;
+  if (int rc = ps_shape(m, n, k, p, std::max(1, d->sms / 2), &bound)) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(muse::kPkThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(muse::ps_smem(bound.t, bound.stages));
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = (p.flags & MUSE_FLAG_PDL) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cfg.gridDim = dim3(2, 1, 1);
+  int clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+  if (e != cudaSuccess || clusters < 1)
+    return fail(MUSE_ERR_PLAN, "tc_pairk stream-K: CTA pairs cannot be scheduled (%s)",
+                e == cudaSuccess ? "occupancy 0" : cudaGetErrorString(e));
+  // Every pair waits for the others of its tiles: the whole grid must be resident at once.
+  int pairs = p.ctas > 0 ? p.ctas / 2 : clusters;
+  if (pairs > clusters || pairs > d->sms / 2)
+    return fail(MUSE_ERR_PLAN, "tc_pairk stream-K: %d CTA pairs exceed the %d that can be resident at once", pairs,
+                std::min(clusters, d->sms / 2));
+  if (pairs > bound.units) pairs = static_cast<int>(bound.units);  // at most one a unit
+  PsShape sh;
+  if (int rc = ps_shape(m, n, k, p, pairs, &sh)) return rc;
+  if (!scratch || scratch_bytes < bound.scratch)
+    return fail(MUSE_ERR_CAPACITY, "tc_pairk stream-K needs %lld bytes of zeroed scratch (got %lld)", (long long)bound.scratch,
+                (long long)(scratch ? scratch_bytes : 0));
+  if (reinterpret_cast<uintptr_t>(scratch) & 255u) return fail(MUSE_ERR_ALIGN, "tc_pairk: scratch must be 256-byte aligned");
+  muse::PsArgs a;
+  a.y = static_cast<uint16_t*>(y);
+  a.counters = static_cast<int*>(scratch);
+  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kCounterBytes);
+  a.units = sh.units;
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.T = sh.t;
+  a.stages = sh.stages;
+  a.nkb = sh.nkb;
+  a.rtiles = sh.rtiles;
+  a.ttiles = sh.ttiles;
+  a.cmax = bound.cmax;  // slot stride: the scratch layout muse_scratch_bytes sized
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  CUtensorMap tmx, tmw, tmy;
+  if (int rc = make_map(&tmx, x, m, k, sh.t / 2)) return rc;
+  if (int rc = make_map(&tmw, tiles, static_cast<int64_t>(sh.rtiles) * sh.nkb * 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  // y by 16-row TMA tensor stores where its rows are 16-byte multiples: boxes of 128 columns x 16 tokens.
+  a.tma_y = (n % 8 == 0 && aligned16(y)) ? 1 : 0;
+  std::memset(&tmy, 0, sizeof(tmy));
+  if (a.tma_y) {
+    auto fn = encode_fn();
+    if (!fn) return fail(MUSE_ERR_CUDA, "cuTensorMapEncodeTiled entry point not found");
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(n * 2)};
+    cuuint32_t box[2] = {128u, 16u};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = fn(&tmy, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MUSE_ERR_CUDA, "cuTensorMapEncodeTiled (y) failed (%d)", static_cast<int>(r));
+  }
+  cfg.dynamicSmemBytes = static_cast<size_t>(muse::ps_smem(sh.t, sh.stages));
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, tmx, tmw, tmy, a);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_pairk stream-K launch: %s", cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
 // ---- wide-tile pair GEMM (256 tokens x 512 W rows a CTA pair) -------------------------------------
 
 int run_wide(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p, cudaStream_t st) {
@@ -1521,6 +1650,16 @@ int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, in
     return MUSE_OK;
   }
   if (plan->kernel == MUSE_KERNEL_TC_PAIRK) {
+    if (plan->flags & MUSE_FLAG_STREAMK) {
+      DeviceInfo* d;
+      int sms = 148;
+      if (device_info(&d) == MUSE_OK) sms = d->sms;
+      muse::clear_error();
+      PsShape ps;
+      if (int rc = ps_shape(m, n, k, *plan, std::max(1, sms / 2), &ps)) return rc;
+      *bytes = ps.scratch;
+      return MUSE_OK;
+    }
     PkShape pk;
     if (int rc = pk_shape(m, n, k, *plan, &pk)) return rc;
     *bytes = pk.scratch;
@@ -1554,6 +1693,8 @@ int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, i
   if (plan->kernel == MUSE_KERNEL_TC_ROWS)
     return run_rows(x, tiles, nullptr, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_WIDE) return run_wide(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
+  if (plan->kernel == MUSE_KERNEL_TC_PAIRK && (plan->flags & MUSE_FLAG_STREAMK))
+    return run_pairsk(x, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_PAIRK)
     return run_pairk(x, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
   if (plan->kernel != MUSE_KERNEL_TC_TILE)

@@ -100,6 +100,8 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
             divisor = lambda lim: max(d for d in range(1, max(1, lim) + 1) if t % d == 0)  # the split divides T
             for s in sorted({divisor(smax), divisor(smax // 2)}):
                 out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_PAIRK, tile_n=t, split=s)))
+            if -(-ptiles * nkb // pairs) <= nkb:  # stream-K: equal runs of at most one tile each
+                out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_TC_PAIRK, tile_n=t, flags=_lib.FLAG_STREAMK)))
     if bnt <= 128:
         for stages, ctas in ((4, 2 * sms), (6, sms), (8, sms)):
             if bnt >= 128 and ctas > sms:

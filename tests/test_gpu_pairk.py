@@ -93,3 +93,40 @@ def test_pairk_refuses_split_grid_beyond_one_wave():
     with pytest.raises(_lib.MuseError, match="resident"):
         _lib.proj_bf16_tiles(x.data_ptr(), t.data_ptr(), y.data_ptr(), m, n, k, pk_plan(256, 2), stream(), big.data_ptr(),
                              big.numel())
+
+
+SK_CASES = [
+    # (m, n, k, tile_n, ctas): the stream-K schedule (equal runs of (tile, k block) units, one a pair)
+    (256, 10240, 8192, 256, 0),   # 40 tiles for 74 pairs: runs of 69 of a tile's 128 k blocks
+    (128, 6144, 4096, 128, 0),    # 24 tiles
+    (256, 2304, 8192, 256, 0),    # 9 tiles: about 9 contributors a tile
+    (256, 8192, 1024, 128, 0),    # two token tiles, runs of 13-14 of 16 k blocks
+    (200, 1000, 640, 208, 40),    # ragged, 20 pairs; the tensor store clips the edges
+    (100, 3000, 4160, 112, 60),   # ragged K, 30 pairs
+    (64, 1001, 1024, 64, 20),     # N not a multiple of 8: plain stores
+    (33, 2304, 8192, 48, 0),      # 48 tokens in 16-token slices: some contributors reduce nothing
+]
+
+
+@pytest.mark.parametrize("m,n,k,t,ctas", SK_CASES)
+def test_pairk_streamk_parity(m, n, k, t, ctas):
+    xb, wb = _rand_bits((m, k), 41 + m + k), _rand_bits((n, k), 43 + n, 0.02)
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_PAIRK, tile_n=t, ctas=ctas, flags=_lib.FLAG_STREAMK)
+    y = _run_bf16(xb, wb, plan, tiles=True)
+    torch.cuda.synchronize()
+    assert _lib.device_error(stream()) == 0
+    assert_parity(xb, wb, y, what=f"tc_pairk stream-K m={m} n={n} k={k} tile_n={t} ctas={ctas}")
+    assert int(scratch_buf()[:65536].count_nonzero()) == 0
+    again = _run_bf16(xb, wb, plan, tiles=True)  # deterministic: the same grid sums in the same order
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), again.view(torch.int16))
+
+
+def test_pairk_streamk_refuses_runs_longer_than_a_tile():
+    m, n, k = 512, 57344, 8192  # 448 tiles of 128 k blocks for 74 pairs
+    x = torch.zeros((m, k), dtype=torch.bfloat16, device="cuda")
+    t = torch.zeros(_lib.tiles_bytes(n, k), dtype=torch.uint8, device="cuda")
+    y = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_PAIRK, tile_n=256, flags=_lib.FLAG_STREAMK)
+    with pytest.raises(_lib.MuseError, match="exceed a tile"):
+        _lib.proj_bf16_tiles(x.data_ptr(), t.data_ptr(), y.data_ptr(), m, n, k, plan, stream(), 0, 0)
