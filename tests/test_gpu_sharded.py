@@ -59,8 +59,13 @@ def _worker(rank, world, port, results):
             wb = w.view(torch.int16).numpy().view(np.uint16)
             ok, msg, _ = O.check_implementation(xb, wb, y_full.cpu().view(torch.int16).numpy().view(np.uint16))
             per = n // world
-            same = torch.equal(y_cols.cpu().view(torch.int16), y_full.cpu()[:, rank * per:(rank + 1) * per].view(torch.int16))
-            out[("row", m, n, k)] = (ok and same, msg)
+            # The reduce-scatter and the all-reduce may add the ranks' FP32 partials in different orders
+            # (NCCL picks the algorithm), so the BF16 results may differ by a rounding step: one unit in
+            # the last place of BF16 (2^-8 relative; near zero, FP32 rounding of the partials' scale).
+            cols = y_cols.cpu().float()
+            ref = y_full.cpu()[:, rank * per:(rank + 1) * per].float()
+            same = bool(((cols - ref).abs() <= ref.abs() * 2.0 ** -7 + 1e-5 * ref.abs().max()).all())
+            out[("row", m, n, k)] = (ok and same, msg if ok else msg + "; column slice differs beyond one BF16 step")
         results[rank] = out
     finally:
         dist.destroy_process_group()
