@@ -563,12 +563,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
-// 16-byte store of output that no kernel of this launch reads again: streaming (evict-first in L2),
-// so a GEMM's y does not push the operand tiles it re-reads out of L2.
-__device__ __forceinline__ void st_cs_v4(void* p, uint4 v) {
-  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
-}
-
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 v;
   asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"

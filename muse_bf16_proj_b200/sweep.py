@@ -186,6 +186,36 @@ class ShapeBench:
         return batch, statistics.mean(a.elapsed_time(b) * 1e3 for a, b in evs)
 
 
+    def one_call_us(self, m: int, fmt: str, plan: _lib.MusePlan, reps: int) -> float:
+        """One launch timed as the reference's judge times a call (validate.py:124-147): captured in a
+        CUDA graph, a 256 MB read to flush L2, then the replay between two events; the mean over `reps`
+        (the event clock ticks in 2.048 us steps, which the replays' random phase resolves in a mean)."""
+        if getattr(self, "flush", None) is None:
+            self.flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+        cur = torch.cuda.current_stream()
+        side = torch.cuda.Stream()
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            self.launch(0, m, fmt, plan)
+            self.launch(0, m, fmt, plan)
+        cur.wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.launch(0, m, fmt, plan)
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(reps):
+            self.flush.sum()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(cur)
+            g.replay()
+            b.record(cur)
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b) * 1e3)
+        del g
+        return statistics.fmean(times)
+
     def cublas_us(self, m: int, reps: int) -> float:
         """Back-to-back microseconds per call of torch's F.linear (cuBLAS) on the same rotating
         weights and inputs: the reference's scoring baseline (baseline.py:56-60, restated as
@@ -252,7 +282,7 @@ def trace_plan(sb: "ShapeBench", m: int, fmt: str, plan: _lib.MusePlan, log, lau
     return {"launches": per, "raw": raws}
 
 
-def sweep_shape(n, k, ms, reps, sms, twelve, log, only=None, trace=False, extra_flags=0, kernels=None):
+def sweep_shape(n, k, ms, reps, sms, twelve, log, only=None, trace=False, extra_flags=0, kernels=None, one_call=0):
     sb = ShapeBench(n, k, max(ms), twelve)
     rows = []
     for m in ms:
@@ -272,11 +302,14 @@ def sweep_shape(n, k, ms, reps, sms, twelve, log, only=None, trace=False, extra_
                 log(f"  n={n} k={k} m={m} {fmt} {plan.as_dict()}: WRONG rel {err:.3e}")
                 continue
             med, mean = sb.time_us(m, fmt, plan, reps)
+            one = sb.one_call_us(m, fmt, plan, one_call) if one_call else None
+            if one is not None:
+                log(f"  n={n} k={k} m={m} {fmt} {plan.as_dict()}: {med:.2f} us back to back, one call {one:.2f} us")
             tr = trace_plan(sb, m, fmt, plan, log) if trace else None
             wbytes = n * k * (1.5 if fmt == "12b" else 2)
             gbs = (wbytes + m * k * 2 + m * n * 2) / (med * 1e-6) / 1e9
             results.append({"fmt": fmt, "plan": plan.as_dict(), "us": med, "us_mean": mean, "gbs": gbs, "rel": err,
-                            "trace": tr})
+                            "one_call_us": one, "trace": tr})
         results.sort(key=lambda r: r["us"])
         best16 = next((r for r in results if r["fmt"] == "bf16"), None)
         cub = sb.cublas_us(m, reps)
@@ -349,6 +382,8 @@ def main():
     ap.add_argument("--trace", action="store_true", help="also record per-CTA timestamps of each plan")
     ap.add_argument("--flags", type=int, default=0, help="plan flags OR-ed into every candidate (2 = PDL)")
     ap.add_argument("--kernels", default="", help="comma-separated kernel names: time only their candidates")
+    ap.add_argument("--one-call", type=int, default=0, metavar="REPS",
+                    help="also time each candidate as one call the judge's way (graph replay after an L2 flush), mean of REPS")
     ap.add_argument("--from-json", default="", help="write the table from an earlier sweep's JSON (no GPU)")
     args = ap.parse_args()
     if args.from_json:
@@ -387,7 +422,7 @@ def main():
         if not shape_ms:
             continue
         rows += sweep_shape(n, k, shape_ms, args.reps, sms, not args.no_12b, log, only, args.trace, args.flags,
-                            set(args.kernels.split(",")) if args.kernels else None)
+                            set(args.kernels.split(",")) if args.kernels else None, args.one_call)
     os.makedirs(os.path.dirname(args.out) or ".", exist_ok=True)
     with open(args.out, "w") as f:
         json.dump({"device": torch.cuda.get_device_name(), "sms": sms, "rows": rows,
