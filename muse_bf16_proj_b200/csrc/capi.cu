@@ -1026,7 +1026,9 @@ int run_wide(const void* x, const void* tiles, void* y, int64_t m, int64_t n, in
   if (m > (int64_t(1) << 24) || n > (int64_t(1) << 24) || k > (int64_t(1) << 24))
     return fail(MUSE_ERR_SHAPE, "tc_wide: dimension too large");
   const int limit = std::min(kSmemLimit, d->smem_optin);
-  const int max_stages = (limit - 1024 - 128) / (muse::kWdStage + 16);
+  // y by TMA tensor stores from a 32 KB staging tile where its rows are 16-byte multiples.
+  const bool tma_y = n % 8 == 0 && aligned16(y);
+  const int max_stages = (limit - 1024 - 128 - (tma_y ? muse::kWdStg : 0)) / (muse::kWdStage + 16);
   const int stages = p.stages > 0 ? p.stages : max_stages;
   if (stages < 2 || stages > max_stages) return fail(MUSE_ERR_PLAN, "tc_wide: %d stages do not fit (max %d)", stages, max_stages);
   if (p.split < 0) return fail(MUSE_ERR_PLAN, "tc_wide: split (token tiles a group) must be >= 0");
@@ -1044,12 +1046,18 @@ int run_wide(const void* x, const void* tiles, void* y, int64_t m, int64_t n, in
   // 6.01 ms, of 8: 6.44 ms).
   a.group_m = p.split > 0 ? std::min(p.split, a.mtiles)
                           : static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(a.mtiles, (64ll << 20) / (512 * k))));
+  a.tma_y = tma_y ? 1 : 0;
   a.trace = g_trace.load();
   a.trace_cap = a.trace ? g_trace_cap.load() : 0;
   const long long tiles_total = static_cast<long long>(a.mtiles) * a.ntiles;
   const long long tile_rows = static_cast<long long>(a.rtiles) * a.nkb * 128;
   if (tiles_total > INT32_MAX || tile_rows > INT32_MAX) return fail(MUSE_ERR_SHAPE, "tc_wide: too many tiles");
-  CUtensorMap tmx, tmw;
+  CUtensorMap tmx, tmw, tmy;
+  std::memset(&tmy, 0, sizeof(tmy));
+  // y seen as [M, N] BF16, boxes of 64 columns x 128 rows, 128-byte swizzle (the staging tile's order).
+  if (tma_y) {
+    if (int rc = make_map(&tmy, y, m, n, 128)) return rc;
+  }
   if (int rc = make_map(&tmx, x, m, k, 128)) return rc;
   // The packed tile array seen as [tiles * 128 rows, 64] BF16: a box is one 16 KB tile, copied as is.
   if (int rc = make_map(&tmw, tiles, tile_rows, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE)) return rc;
@@ -1065,7 +1073,7 @@ int run_wide(const void* x, const void* tiles, void* y, int64_t m, int64_t n, in
   }
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(muse::kWdThreads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(muse::wd_smem(stages));
+  cfg.dynamicSmemBytes = static_cast<size_t>(muse::wd_smem(stages, tma_y));
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1084,7 +1092,7 @@ int run_wide(const void* x, const void* tiles, void* y, int64_t m, int64_t n, in
   long long pairs = p.ctas > 0 ? p.ctas / 2 : clusters;
   pairs = std::max<long long>(1, std::min<long long>({pairs, static_cast<long long>(clusters), tiles_total}));
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, tmx, tmw, a);
+  e = cudaLaunchKernelEx(&cfg, kern, tmx, tmw, tmy, a);
   if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_wide launch: %s", cudaGetErrorString(e));
   return MUSE_OK;
 }

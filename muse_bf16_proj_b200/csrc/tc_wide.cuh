@@ -32,13 +32,17 @@ constexpr int kWdStage = 3 * kWdHalf;  // x, W half 0, W half 1 (per CTA)
 constexpr uint32_t kWdCols = 512;
 constexpr unsigned int kErrWdProducer = 0x801, kErrWdMma = 0x802, kErrWdEpilogue = 0x803;
 
-__host__ __device__ constexpr int wd_smem(int stages) { return 1024 + stages * kWdStage + (2 * stages + 6) * 8 + 32; }
+constexpr int kWdStg = 32768;  // y staging for the tensor-store epilogue: 128 token rows x 128 W rows of BF16
+__host__ __device__ constexpr int wd_smem(int stages, bool tma_y = false) {
+  return 1024 + stages * kWdStage + (tma_y ? kWdStg : 0) + (2 * stages + 6) * 8 + 32;
+}
 
 struct WdArgs {
   uint16_t* y;  // [M, N]
   int M, N, stages;
   int mtiles, ntiles, nkb, rtiles;  // 256-token tiles, 512-row tiles, k blocks, 128-row packed tiles
   int group_m;                      // token tiles walked together
+  int tma_y;                        // 1: y written by TMA tensor stores from a staging tile (N % 8 == 0)
   TraceRec* trace;
   int trace_cap;
 };
@@ -53,7 +57,8 @@ __device__ __forceinline__ void wd_tile_coords(const WdArgs& a, int t, int& mt, 
 }
 
 __global__ void __launch_bounds__(kWdThreads, 1)
-    tc_wide_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, const WdArgs a) {
+    tc_wide_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+                   const __grid_constant__ CUtensorMap tmy, const WdArgs a) {
   constexpr uint32_t kIdesc = umma_idesc_bf16(256, 256);
   extern __shared__ uint8_t smem_raw[];
   const bool tracing = a.trace != nullptr && static_cast<int>(blockIdx.x) < a.trace_cap && threadIdx.x == 64;
@@ -61,12 +66,15 @@ __global__ void __launch_bounds__(kWdThreads, 1)
   unsigned long long t_ready = 0ull, t_main = 0ull;
   uint8_t* smem = smem_align<1024>(smem_raw);
   const int stages = a.stages;
-  // Stage s: x at s * 48 KB, W half 0 at + 16 KB, W half 1 at + 32 KB.
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(stages) * kWdStage);
+  // Stage s: x at s * 48 KB, W half 0 at + 16 KB, W half 1 at + 32 KB; then (tma_y) the y staging tile:
+  // two 16 KB sub-tiles of 128 token rows x 64 W rows in the 128-byte-swizzled order of the y map.
+  uint8_t* ystg = smem + static_cast<size_t>(stages) * kWdStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ystg + (a.tma_y ? kWdStg : 0));
   uint64_t* empty = full + stages;
   uint64_t* acc_full = empty + stages;  // [1] both accumulators of a tile complete
   uint64_t* acc_empty = acc_full + 1;   // [2] accumulator h drained (even CTA: 4 local + 4 remote arrives)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* epi_abort = reinterpret_cast<int*>(tmem_slot + 1);  // tma_y: an epilogue warp's accumulator wait failed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -78,6 +86,7 @@ __global__ void __launch_bounds__(kWdThreads, 1)
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmx);
     prefetch_tensormap(&tmw);
+    if (a.tma_y) prefetch_tensormap(&tmy);
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -85,6 +94,7 @@ __global__ void __launch_bounds__(kWdThreads, 1)
     mbar_init(acc_full, 1);
     mbar_init(&acc_empty[0], 8);
     mbar_init(&acc_empty[1], 8);
+    *epi_abort = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, kWdCols);
@@ -197,7 +207,12 @@ __global__ void __launch_bounds__(kWdThreads, 1)
     for (int t = pair; t < tiles; t += npairs, ++local) {
       int mt, nt;
       wd_tile_coords(a, t, mt, nt);
-      const bool ok = __all_sync(0xffffffffu, mbar_wait_idle(acc_full, static_cast<uint32_t>(local & 1), kErrWdEpilogue));
+      bool ok = __all_sync(0xffffffffu, mbar_wait_idle(acc_full, static_cast<uint32_t>(local & 1), kErrWdEpilogue));
+      if (a.tma_y) {  // the four warps share named barriers below: the same answer in all of them
+        if (!ok && lane == 0) *epi_abort = 1;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        ok = *reinterpret_cast<volatile int*>(epi_abort) == 0;
+      }
       tc_fence_after();
       if (!waited) {
         if (tracing) t_main = globaltimer();
@@ -210,6 +225,37 @@ __global__ void __launch_bounds__(kWdThreads, 1)
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         const int n0 = nt * 512 + h * 256;
+        if (a.tma_y) {
+          // Two rounds of 128 W rows: TMEM -> BF16 -> the swizzled staging tile -> two tensor stores
+          // (rows and columns past M and N clipped by the store). The staging is reused only after the
+          // previous round's stores have read it.
+          const uint32_t stg = smem_u32(ystg);
+#pragma unroll 1
+          for (int r = 0; r < 2; ++r) {
+            if (threadIdx.x == 64) bulk_wait_read_all();
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll 1
+            for (int cc = 0; cc < 4; ++cc) {  // 32 W rows each: sub-tile cc / 2, 16-byte chunks 4 (cc % 2) .. + 3
+              float v[32];
+              tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(h * 256 + r * 128 + cc * 32), v);
+              const uint32_t sub = stg + static_cast<uint32_t>((cc >> 1) * 16384 + row * 128);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t chunk = static_cast<uint32_t>(((cc & 1) * 4 + j) ^ (row & 7));
+                st_shared_v4u(sub + chunk * 16u, pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                              pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+              }
+            }
+            fence_proxy_async_shared();  // the staged rows before the tensor stores read them
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (threadIdx.x == 64) {
+              const int row0 = mt * 256 + static_cast<int>(rank) * 128;
+              tma_store_2d(&tmy, ystg, n0 + r * 128, row0);
+              tma_store_2d(&tmy, ystg + 16384, n0 + r * 128 + 64, row0);
+              bulk_commit();
+            }
+          }
+        } else {
 #pragma unroll 1
         for (int c = 0; c < 256; c += 32) {
           float v[32];
@@ -229,12 +275,14 @@ __global__ void __launch_bounds__(kWdThreads, 1)
             }
           }
         }
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(map_peer(smem_u32(&acc_empty[h]), 0u));
       }
     }
     if (!waited) pdl_wait();
+    if (a.tma_y && threadIdx.x == 64) bulk_wait_all();  // every tensor store of y has completed
   }
   pdl_launch_dependents();
 
