@@ -66,6 +66,11 @@ extern "C" {
  * once and runs of at most one tile (the host refuses other grids); each contributor of a tile reduces
  * a 16-token-aligned slice of it. */
 #define MUSE_FLAG_STREAMK 4
+/* TC_GEMM2: the whole waves of 256 x 256 tiles run persistently and only the tiles left over after the
+ * last whole wave of CTA pairs run stream-K (their units cut into equal runs over every pair, summed
+ * from partials in scratch by each tile's last contributor in a fixed order), so the last wave leaves no
+ * pair idle. Excludes MUSE_FLAG_STREAMK. */
+#define MUSE_FLAG_SK_TAIL 8
 
 /* How one projection runs. Zero fields take the kernel's default. */
 typedef struct MusePlan {

@@ -30,6 +30,7 @@ KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
 FLAG_GLOBAL_SPLIT = 1
 FLAG_PDL = 2
 FLAG_STREAMK = 4
+FLAG_SK_TAIL = 8
 
 
 class MuseError(RuntimeError):

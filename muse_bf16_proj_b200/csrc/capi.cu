@@ -656,17 +656,30 @@ int run_gemm(const void* x, const void* tiles, void* y, int64_t m, int64_t n, in
 
 // ---- persistent prefill GEMM over CTA pairs --------------------------------------------------
 
-// Stream-K scratch of the pair GEMM: 64 KB of tickets, then the partials of tiles shared by up to
-// smax pairs ([tile][contributor][CTA] of 128 KB). smax is sized for the most pairs the device can
-// run (fewer pairs only lengthen each pair's run, so fewer share a tile).
-int64_t g2_sk_scratch(int64_t m, int64_t n, int64_t k, int sms, int* smax_out) {
+// Stream-K layout of the pair GEMM for `pairs` CTA pairs: the first stream-K tile (0: all; with
+// `tail`, the tiles after the last whole wave of pairs: the whole waves run persistently), the most
+// pairs sharing a stream-K tile, and the scratch: 64 KB of tickets, then the partials of the stream-K
+// tiles ([tile][contributor][CTA] of 128 KB). Returns the bytes; *tile0 == tiles: nothing to share.
+int64_t g2_sk_layout(int64_t m, int64_t n, int64_t k, int64_t pairs, bool tail, int64_t* tile0, int* smax_out) {
   const int64_t tiles = ((m + 255) / 256) * ((n + 255) / 256);
   const int64_t nkb = (k + 63) / 64;
-  const int64_t pairs = std::max(1, sms / 2);
-  const int64_t minrange = std::max<int64_t>(1, tiles * nkb / pairs);
+  pairs = std::max<int64_t>(1, pairs);
+  const int64_t t0 = tail ? tiles / pairs * pairs : 0;
+  const int64_t sk_tiles = tiles - t0;
+  const int64_t minrange = std::max<int64_t>(1, sk_tiles * nkb / pairs);
   const int smax = static_cast<int>((nkb + minrange - 1) / minrange + 1);
+  if (tile0) *tile0 = t0;
   if (smax_out) *smax_out = smax;
-  return kCounterBytes + tiles * smax * 2 * 128 * 256 * 4;
+  return sk_tiles ? kCounterBytes + sk_tiles * smax * 2 * 128 * 256 * 4 : 0;
+}
+
+// Scratch for a stream-K plan of the pair GEMM on a device of `sms` SMs: the most any pair count up to
+// sms / 2 needs (more pairs share a tile more ways; with a tail, fewer pairs can leave a longer tail).
+int64_t g2_sk_scratch(int64_t m, int64_t n, int64_t k, int sms, bool tail) {
+  int64_t need = 0;
+  const int64_t hi = std::max(1, sms / 2);
+  for (int64_t p = tail ? 1 : hi; p <= hi; ++p) need = std::max(need, g2_sk_layout(m, n, k, p, tail, nullptr, nullptr));
+  return need;
 }
 
 // g != nullptr: the all-gather epilogue (y unused; every value goes to each rank's y_full).
@@ -707,22 +720,13 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
   if (g) a.g = *g;
   a.streamk = 0;
   a.smax = 0;
+  a.sk_tile0 = 0;
   a.partials = nullptr;
   a.counters = nullptr;
-  if (p.flags & MUSE_FLAG_STREAMK) {
-    if (g) return fail(MUSE_ERR_PLAN, "tc_gemm2: the fused all-gather runs the persistent (not stream-K) schedule");
-    int smax = 0;
-    const int64_t need = g2_sk_scratch(m, n, k, d->sms, &smax);
-    if (!scratch || scratch_bytes < need)
-      return fail(MUSE_ERR_CAPACITY, "tc_gemm2: stream-K needs %lld bytes of zeroed scratch (got %lld)", (long long)need,
-                  (long long)(scratch ? scratch_bytes : 0));
-    if (reinterpret_cast<uintptr_t>(scratch) & 255u) return fail(MUSE_ERR_ALIGN, "tc_gemm2: scratch must be 256-byte aligned");
-    if (tiles_total * 2 > kMaxCounters) return fail(MUSE_ERR_SHAPE, "tc_gemm2: too many tiles for stream-K");
-    a.streamk = 1;
-    a.smax = smax;
-    a.counters = static_cast<int*>(scratch);
-    a.partials = reinterpret_cast<float4*>(static_cast<uint8_t*>(scratch) + kCounterBytes);
-  }
+  const bool sk_all = (p.flags & MUSE_FLAG_STREAMK) != 0, sk_tail = (p.flags & MUSE_FLAG_SK_TAIL) != 0;
+  if ((sk_all || sk_tail) && g)
+    return fail(MUSE_ERR_PLAN, "tc_gemm2: the fused all-gather runs the persistent (not stream-K) schedule");
+  if (sk_all && sk_tail) return fail(MUSE_ERR_PLAN, "tc_gemm2: MUSE_FLAG_STREAMK and MUSE_FLAG_SK_TAIL exclude each other");
   CUtensorMap tmx, tmw;
   if (int rc = make_map(&tmx, x, m, k, 128)) return rc;
   // The packed tile array seen as [tiles * 128 rows, 64] BF16: a box is one 16 KB tile, copied as is.
@@ -757,8 +761,29 @@ int run_gemm2(const void* x, const void* tiles, void* y, int64_t m, int64_t n, i
     return fail(MUSE_ERR_PLAN, "tc_gemm2: CTA pairs cannot be scheduled (%s)", e == cudaSuccess ? "occupancy 0" : cudaGetErrorString(e));
   long long pairs = p.ctas > 0 ? p.ctas / 2 : clusters;
   // Persistent tiles: no more pairs than tiles. Stream-K: every resident pair (up to one k block each).
-  const long long cap = a.streamk ? tiles_total * a.nkb : tiles_total;
+  const long long cap = sk_all ? tiles_total * a.nkb : tiles_total;
   pairs = std::max<long long>(1, std::min<long long>({pairs, static_cast<long long>(clusters), cap}));
+  if (sk_all || sk_tail) {
+    // The stream-K tiles' pairs wait for no one (the last contributor of a tile sums it), but the
+    // scratch was sized for at most sms / 2 pairs.
+    pairs = std::min<long long>(pairs, std::max(1, d->sms / 2));
+    int64_t tile0 = 0;
+    int smax = 0;
+    const int64_t need = g2_sk_layout(m, n, k, pairs, sk_tail, &tile0, &smax);
+    if (tile0 < tiles_total) {
+      if (!scratch || scratch_bytes < need)
+        return fail(MUSE_ERR_CAPACITY, "tc_gemm2: stream-K needs %lld bytes of zeroed scratch (got %lld)", (long long)need,
+                    (long long)(scratch ? scratch_bytes : 0));
+      if (reinterpret_cast<uintptr_t>(scratch) & 255u)
+        return fail(MUSE_ERR_ALIGN, "tc_gemm2: scratch must be 256-byte aligned");
+      if ((tiles_total - tile0) * 2 > kMaxCounters) return fail(MUSE_ERR_SHAPE, "tc_gemm2: too many tiles for stream-K");
+      a.streamk = 1;
+      a.smax = smax;
+      a.sk_tile0 = static_cast<int>(tile0);
+      a.counters = static_cast<int*>(scratch);
+      a.partials = reinterpret_cast<float4*>(static_cast<uint8_t*>(scratch) + kCounterBytes);
+    }
+  }
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   e = cudaLaunchKernelEx(&cfg, kern, tmx, tmw, a);
   if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "tc_gemm2 launch: %s", cudaGetErrorString(e));
@@ -1648,12 +1673,12 @@ int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, in
     return MUSE_OK;
   }
   if (plan->kernel == MUSE_KERNEL_TC_GEMM2) {
-    if (plan->flags & MUSE_FLAG_STREAMK) {
+    if (plan->flags & (MUSE_FLAG_STREAMK | MUSE_FLAG_SK_TAIL)) {
       DeviceInfo* d;
       int sms = 148;
       if (device_info(&d) == MUSE_OK) sms = d->sms;
       muse::clear_error();
-      *bytes = g2_sk_scratch(m, n, k, sms, nullptr);
+      *bytes = g2_sk_scratch(m, n, k, sms, (plan->flags & MUSE_FLAG_SK_TAIL) != 0);
     }
     return MUSE_OK;
   }

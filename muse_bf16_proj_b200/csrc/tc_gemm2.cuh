@@ -46,8 +46,12 @@ struct G2Args {
   // shared by several pairs leaves FP32 partials in `partials` ([tile][contributor][CTA][64][128]
   // float4: column quad c of row r at c * 128 + r) and its last contributor adds them in order.
   int streamk, smax;
+  // Tiles below sk_tile0 are walked persistently (whole tiles, no partials); stream-K covers the
+  // units of the tiles from sk_tile0 on (0: every tile). A tile's partials and counters are indexed
+  // from sk_tile0.
+  int sk_tile0;
   float4* partials;
-  int* counters;  // [tiles][2], zero between launches
+  int* counters;  // [tiles - sk_tile0][2], zero between launches
 };
 
 // Tile t's coordinates in the grouped order: groups of `group_m` token tiles (the last one
@@ -64,32 +68,34 @@ __device__ __forceinline__ void g2_tile_coords(const G2Args& a, int t, int& mt, 
   nt = w / gm;
 }
 
-// The segments one pair computes, in order: whole tiles pair, pair + npairs, ... (persistent), or
-// under stream-K the pair's run of (tile, k block) units cut at tile boundaries.
+// The segments one pair computes, in order: whole tiles pair, pair + npairs, ... below the stream-K
+// start (all tiles without stream-K), then under stream-K the pair's run of the remaining
+// (tile, k block) units cut at tile boundaries.
 struct G2Segs {
   long long u, u1;
-  int t, step, tiles, nkb;
+  int t, step, t_end, nkb;
   bool sk;
   __device__ G2Segs(const G2Args& a, int pair, int npairs) {
-    tiles = a.mtiles * a.ntiles;
+    const int tiles = a.mtiles * a.ntiles;
     nkb = a.nkb;
     sk = a.streamk != 0;
     t = pair;
     step = npairs;
-    const long long units = static_cast<long long>(tiles) * nkb;
-    u = sk ? t12_start(pair, units, npairs) : 0;
-    u1 = sk ? t12_start(pair + 1, units, npairs) : 0;
+    t_end = sk ? a.sk_tile0 : tiles;
+    const long long base = static_cast<long long>(a.sk_tile0) * nkb;
+    const long long units = static_cast<long long>(tiles) * nkb - base;
+    u = sk ? base + t12_start(pair, units, npairs) : 0;
+    u1 = sk ? base + t12_start(pair + 1, units, npairs) : 0;
   }
   __device__ bool next(int& tile, int& kb0, int& kb1) {
-    if (!sk) {
-      if (t >= tiles) return false;
+    if (t < t_end) {
       tile = t;
       kb0 = 0;
       kb1 = nkb;
       t += step;
       return true;
     }
-    if (u >= u1) return false;
+    if (!sk || u >= u1) return false;
     tile = static_cast<int>(u / nkb);
     kb0 = static_cast<int>(u - static_cast<long long>(tile) * nkb);
     kb1 = static_cast<int>(min(static_cast<long long>(nkb), kb0 + (u1 - u)));
@@ -253,10 +259,12 @@ __global__ void __launch_bounds__(kG2Threads, 1)
         // Part of a tile shared with other pairs: park this CTA's 128 x 256 FP32 partial, release
         // the accumulator, take the tile's ticket; the last contributor adds every partial in
         // contributor order and stores BF16.
-        const long long units = static_cast<long long>(tiles) * nkb;
-        const int first = t12_owner(static_cast<long long>(t) * nkb, units, npairs);
-        const int nseg = t12_owner(static_cast<long long>(t + 1) * nkb - 1, units, npairs) - first + 1;
-        float4* tp = a.partials + static_cast<size_t>(t) * a.smax * 2 * 64 * 128;  // this tile's partials
+        const long long base = static_cast<long long>(a.sk_tile0) * nkb;
+        const long long units = static_cast<long long>(tiles) * nkb - base;
+        const int first = t12_owner(static_cast<long long>(t) * nkb - base, units, npairs);
+        const int nseg = t12_owner(static_cast<long long>(t + 1) * nkb - 1 - base, units, npairs) - first + 1;
+        const int ts = t - a.sk_tile0;  // this tile among the stream-K ones
+        float4* tp = a.partials + static_cast<size_t>(ts) * a.smax * 2 * 64 * 128;  // this tile's partials
         float4* mine = tp + (static_cast<size_t>(pair - first) * 2 + rank) * 64 * 128;
 #pragma unroll 1
         for (int c = 0; c < 256; c += 16) {
@@ -270,7 +278,7 @@ __global__ void __launch_bounds__(kG2Threads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(map_peer(smem_u32(&acc_empty[b]), 0u));
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (row == 0) epi_flag[1] = (ticket_acq_rel(a.counters + t * 2 + static_cast<int>(rank)) == nseg - 1) ? 1 : 0;
+        if (row == 0) epi_flag[1] = (ticket_acq_rel(a.counters + ts * 2 + static_cast<int>(rank)) == nseg - 1) ? 1 : 0;
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (epi_flag[1]) {
           const float4* part = tp + static_cast<size_t>(rank) * 64 * 128 + row;
@@ -310,7 +318,7 @@ __global__ void __launch_bounds__(kG2Threads, 1)
               }
             }
           }
-          if (row == 0) a.counters[t * 2 + static_cast<int>(rank)] = 0;  // as the next launch expects it
+          if (row == 0) a.counters[ts * 2 + static_cast<int>(rank)] = 0;  // as the next launch expects it
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");  // epi_flag[1] is rewritten by the next segment
         continue;

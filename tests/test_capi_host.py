@@ -181,6 +181,10 @@ def test_stream_k_scratch_sizing_and_plan_errors():
     need = _lib.scratch_bytes(256, 10240, 8192, sk)
     assert need > 65536 and (need - 65536) % (2 * 128 * 256 * 4) == 0  # whole 128 KB tile halves
     assert _lib.scratch_bytes(256, 10240, 8192, _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2)) == 0
+    tail = _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2, flags=_lib.FLAG_SK_TAIL)
+    need = _lib.scratch_bytes(8192, 7168, 8192, tail)  # 896 tiles: a tail after the whole waves
+    assert need > 65536 and (need - 65536) % (2 * 128 * 256 * 4) == 0
+    assert need < _lib.scratch_bytes(8192, 7168, 8192, sk)  # only the tail's tiles have partials
 
 
 def test_device_encoder_argument_errors():

@@ -457,6 +457,39 @@ def test_tc_gemm_pairs_streamk(m, n, k, ctas):
     assert_parity(xb, wb, ys[0], what=f"gemm2 stream-K m={m} n={n} k={k} ctas={ctas}")
     assert torch.equal(ys[0].view(torch.int16), ys[1].view(torch.int16)), "not deterministic"
     assert int(sc[:65536].view(torch.int32).abs().sum()) == 0, "tickets not left at zero"
-    with pytest.raises(_lib.MuseError):  # scratch too small
-        _lib.proj_bf16_tiles(x.data_ptr(), t.data_ptr(), ys[0].data_ptr(), m, n, k, plan, stream(), sc.data_ptr(),
-                             need - 256)
+    with pytest.raises(_lib.MuseError):  # scratch without room for any partial
+        _lib.proj_bf16_tiles(x.data_ptr(), t.data_ptr(), ys[0].data_ptr(), m, n, k, plan, stream(), sc.data_ptr(), 65536)
+
+
+SK_TAIL_CASES = [
+    (2048, 4608, 2048, 0),    # 144 tiles: one whole wave of 74 pairs, then 70 tiles stream-K (2-3 pairs a tile)
+    (2560, 7424, 1024, 0),    # 290 tiles: three whole waves, 68 tiles stream-K
+    (1024, 2816, 1024, 0),    # 44 tiles, fewer than the pairs: no whole wave, every tile stream-K
+    (1024, 3000, 2048, 20),   # 10 pairs: four whole waves, 8 tiles stream-K; ragged N (scalar stores)
+    (2048, 9472, 1024, 0),    # 296 tiles = four whole waves: nothing left for stream-K
+]
+
+
+@pytest.mark.parametrize("m,n,k,ctas", SK_TAIL_CASES)
+def test_tc_gemm_pairs_streamk_tail(m, n, k, ctas):
+    """The pair GEMM with a stream-K tail (MUSE_FLAG_SK_TAIL): whole waves of tiles persistently, the
+    tiles left after the last whole wave as equal runs over every pair, summed from FP32 partials by
+    each tile's last contributor; deterministic, tickets left at zero, bit for bit the same sums as
+    the persistent schedule where a tile is not shared."""
+    xb, wb = _rand_bits((m, k), 310 + m), _rand_bits((n, k), 315 + n, 0.02)
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_TC_GEMM2, ctas=ctas, flags=_lib.FLAG_SK_TAIL)
+    need = _lib.scratch_bytes(m, n, k, plan)
+    sc = torch.zeros(max(need, 65536), dtype=torch.uint8, device="cuda")
+    x, w = to_dev(xb), to_dev(wb)
+    t = torch.empty(_lib.tiles_bytes(n, k), dtype=torch.uint8, device="cuda")
+    _lib.pack_tiles(w.data_ptr(), t.data_ptr(), n, k, stream())
+    ys = []
+    for _ in range(2):
+        y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        _lib.proj_bf16_tiles(x.data_ptr(), t.data_ptr(), y.data_ptr(), m, n, k, plan, stream(), sc.data_ptr(), sc.numel())
+        ys.append(y)
+    torch.cuda.synchronize()
+    assert _lib.device_error(stream()) == 0
+    assert_parity(xb, wb, ys[0], what=f"gemm2 stream-K tail m={m} n={n} k={k} ctas={ctas}")
+    assert torch.equal(ys[0].view(torch.int16), ys[1].view(torch.int16)), "not deterministic"
+    assert int(sc[:65536].view(torch.int32).abs().sum()) == 0, "tickets not left at zero"
