@@ -51,7 +51,11 @@ extern "C" {
 #define MUSE_KERNEL_TC_WIDE 12
 /* tcgen05 on CTA pairs with W as the A operand: 256 W rows x tile_n tokens a pair, K split `split` ways
  * across pairs that reduce the split together (each sums a slice of the tokens from every partial in
- * scratch, in split order); medium M (about 32 .. 512 tokens). A split grid must fit in one wave. */
+ * scratch, in split order); medium M (about 32 .. 512 tokens). With MUSE_FLAG_STREAMK the (tile, k block)
+ * units are cut into equal runs over every resident pair instead. A split or stream-K grid must fit in one
+ * wave (the host refuses a larger one) because its pairs wait for one another: a pair that cannot be
+ * scheduled within 1 s (another kernel holding SMs indefinitely) ends the launch with device error
+ * 0x904 / 0x914, never a hang. */
 #define MUSE_KERNEL_TC_PAIRK 13
 
 /* Plan flags. */
@@ -81,7 +85,8 @@ typedef struct MusePlan {
   int32_t tile_n; /* tensor-core kernels: tokens per tile, 16/32/64/128 (TC_TILE, TC_STREAMK also 256; TC_PAIRK any
                    * multiple of 16 up to 256) */
   int32_t stages; /* shared-memory ring depth (0 = kernel default) */
-  int32_t ctas;   /* GEMV, TC_STREAMK, TC_SKINNY, TC_12B, TC_ROWS: CTAs in the grid (0 = one per SM) */
+  int32_t ctas;   /* GEMV, TC_STREAMK, TC_SKINNY, TC_12B, TC_ROWS: CTAs in the grid (0 = one per SM); TC_GEMM2,
+                   * TC_WIDE, TC_PAIRK with MUSE_FLAG_STREAMK: 2 x the CTA pairs (0 = every pair that fits) */
   int32_t warps;  /* GEMV: consumer warps per CTA: 4, 8 or 16 (0 = 8) */
   int32_t chunk;  /* GEMV: units per bulk copy (0 = about 16 KB) */
   int32_t flags;  /* MUSE_FLAG_* */
