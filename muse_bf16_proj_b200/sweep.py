@@ -1,7 +1,8 @@
 """Per-shape plan sweep on a B200: times every candidate plan and writes the dispatch table.
 
     python -m muse_bf16_proj_b200.sweep [--shapes reference,baseline] [--ms 1,2,...] [--out path]
-                                        [--write-table] [--reps 40]
+                                        [--write-table] [--reps 40] [--flags 2] [--kernels a,b]
+                                        [--plan JSON] [--trace] [--one-call REPS]
 
 Replaces the reference's Optuna / grid sweeps (sweep_all.py, sweep_cuda.py) with a plain grid: for
 each (N, K, M) every candidate plan is first checked against a torch FP32 product rounded to BF16
@@ -10,7 +11,8 @@ of R weight copies whose total exceeds the 126 MB L2 (every launch reads W cold 
 reference's judge flushes L2). The fastest checked plan per shape becomes a table row; 12-bit
 candidates are timed too and win a row only when faster than every BF16 plan. Every row also
 records cuBLAS (torch F.linear) timed the same way on the same weights: the reference's scoring
-baseline, kept as a comparator (never served).
+baseline, kept as a comparator (never served). --one-call also times each candidate as the reference's
+judge times a call (graph replay after an L2 flush); --trace records per-CTA timestamps and kernel marks.
 """
 
 from __future__ import annotations
