@@ -187,6 +187,27 @@ def test_stream_k_scratch_sizing_and_plan_errors():
     assert need < _lib.scratch_bytes(8192, 7168, 8192, sk)  # only the tail's tiles have partials
 
 
+def test_pair_kernel_plans_and_scratch():
+    """The medium-M pair kernel's plan checks and scratch sizes, on the host (no device work)."""
+    pk = lambda **kw: _lib.MusePlan(kernel=_lib.KERNEL_TC_PAIRK, **kw)
+    # No split: no scratch. A split: 64 KB of counters, then [tiles][2][split][tile_n][128] FP32.
+    assert _lib.scratch_bytes(256, 2304, 8192, pk(tile_n=256, split=1)) == 0
+    assert _lib.scratch_bytes(256, 2304, 8192, pk(tile_n=256, split=8)) == 65536 + 9 * 2 * 8 * 256 * 128 * 4
+    for bad in (pk(tile_n=24), pk(tile_n=272),                  # tile_n a multiple of 16 up to 256;
+                pk(tile_n=256, split=3), pk(tile_n=16, split=32)):  # the split divides tile_n...
+        with pytest.raises(_lib.MuseError) as e:
+            _lib.scratch_bytes(256, 2304, 8192, bad)
+        assert e.value.code == -7
+    with pytest.raises(_lib.MuseError):  # ... and does not exceed the k blocks (K = 1024: 16)
+        _lib.scratch_bytes(256, 2304, 1024, pk(tile_n=256, split=32))
+    # Stream-K: runs of at most one tile, partials for every tile sized for the most contributors.
+    sk = pk(tile_n=256, flags=_lib.FLAG_STREAMK)
+    need = _lib.scratch_bytes(256, 10240, 8192, sk)
+    assert need > 65536 and (need - 65536) % (2 * 256 * 128 * 4) == 0
+    with pytest.raises(_lib.MuseError, match="exceed a tile"):  # 448 tiles for 74 pairs
+        _lib.scratch_bytes(512, 57344, 8192, sk)
+
+
 def test_device_encoder_argument_errors():
     """muse_encode12_device / _escapes reject bad shapes, null or misaligned pointers before any launch."""
     lib = _lib.load()
