@@ -57,6 +57,11 @@ extern "C" {
  * scheduled within 1 s (another kernel holding SMs indefinitely) ends the launch with device error
  * 0x904 / 0x914, never a hang. */
 #define MUSE_KERNEL_TC_PAIRK 13
+/* CUDA-core GEMV over the packed tiles for 1..4 tokens, built for one-call latency: each warp loads 1, 2, 4 or 8
+ * adjacent 4-row quads of one K segment straight into registers (16 loads a lane in flight, the first
+ * issued before the programmatic-launch wait), no ring, barriers, tensor memory or scratch; a CTA's warps
+ * of one quad group add their K segments in segment order. */
+#define MUSE_KERNEL_GEMV_TILES 14
 
 /* Plan flags. */
 #define MUSE_FLAG_GLOBAL_SPLIT 1 /* TC_TILE: reduce K-split partials through caller scratch instead of a cluster */
@@ -81,14 +86,16 @@ typedef struct MusePlan {
   int32_t kernel; /* MUSE_KERNEL_* */
   int32_t split;  /* TC_TILE: CTAs splitting K (cluster: 1..16; global: 1..64); TC_ROWS: 1, 2 or 4 (cluster);
                    * TC_GEMM2, TC_WIDE: 256-token tiles walked together as a group (0 = as many as keep 32 MB of x);
-                   * TC_PAIRK: CTA pairs splitting K (1..64, at most tile_n) */
+                   * TC_PAIRK: CTA pairs splitting K (1..64, at most tile_n); GEMV_TILES: warps splitting each
+                   * 4-row quad's K, a divisor of warps (0 = about 16 k blocks a warp) */
   int32_t tile_n; /* tensor-core kernels: tokens per tile, 16/32/64/128 (TC_TILE, TC_STREAMK also 256; TC_PAIRK any
                    * multiple of 16 up to 256) */
   int32_t stages; /* shared-memory ring depth (0 = kernel default) */
   int32_t ctas;   /* GEMV, TC_STREAMK, TC_SKINNY, TC_12B, TC_ROWS: CTAs in the grid (0 = one per SM); TC_GEMM2,
                    * TC_WIDE, TC_PAIRK with MUSE_FLAG_STREAMK: 2 x the CTA pairs (0 = every pair that fits) */
-  int32_t warps;  /* GEMV: consumer warps per CTA: 4, 8 or 16 (0 = 8) */
-  int32_t chunk;  /* GEMV: units per bulk copy (0 = about 16 KB) */
+  int32_t warps;  /* GEMV: consumer warps per CTA: 4, 8 or 16 (0 = 8); GEMV_TILES: warps per CTA, 1..16 (0 = 8) */
+  int32_t chunk;  /* GEMV: units per bulk copy (0 = about 16 KB); GEMV_TILES: adjacent 4-row quads a warp, 1, 2, 4 or 8
+                   * (8: M <= 2; 0 = 2) */
   int32_t flags;  /* MUSE_FLAG_* */
 } MusePlan;
 
@@ -197,8 +204,10 @@ int muse_pack_tiles(const void* w, void* tiles, int64_t n, int64_t k, void* stre
  * muse_scratch_bytes; TC_SKINNY reads two tiles a k block as one 256-row B operand) or
  * MUSE_KERNEL_TC_GEMM / MUSE_KERNEL_TC_GEMM2 (prefill; replace the cuBLAS F.linear that served
  * the reference's large shapes, submission.py:1170; also MUSE_KERNEL_TC_WIDE), MUSE_KERNEL_TC_PAIRK (medium M; scratch when
- * split > 1; replaces wa_gemm's cluster split-K, submission.py:855-889) or MUSE_KERNEL_TC_ROWS (M <= 128, no scratch;
- * replaces nf12_gemv / wa_gemm at few tokens, submission.py:357-474, 799-890). Each pipeline
+ * split > 1; replaces wa_gemm's cluster split-K, submission.py:855-889), MUSE_KERNEL_TC_ROWS (M <= 128, no scratch;
+ * replaces nf12_gemv / wa_gemm at few tokens, submission.py:357-474, 799-890) or MUSE_KERNEL_GEMV_TILES
+ * (M <= 4, no scratch; the BF16 counterpart of the reference's CUDA-core nf12_gemv, submission.py:357-474, for
+ * decode shapes its Triton bf16_gemm served, submission.py:209-251, 1084-1107). Each pipeline
  * stage moves one contiguous 16 KB tile with a 1-D bulk copy. Replaces TmaGemm.__call__
  * (submission.py:977-988), which read its pre-swizzled W the same way, and the Triton split-K
  * bf16_gemm with its atomic tile tickets (submission.py:209-251, 1084-1107).

@@ -18,14 +18,14 @@ MUSE_OK = 0
 ERRORS = {-1: "INVALID", -2: "ALIGN", -3: "SHAPE", -4: "CAPACITY", -5: "CUDA", -6: "TIMEOUT", -7: "PLAN"}
 KERNEL_GEMV_BF16, KERNEL_GEMV_12B, KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_GEMM, KERNEL_TC_GEMM2 = 1, 2, 3, 4, 5, 6
 KERNEL_TC_12B, KERNEL_TC_SKINNY, KERNEL_F32_GEMV, KERNEL_GEMV_12T, KERNEL_TC_ROWS, KERNEL_TC_WIDE = 7, 8, 9, 10, 11, 12
-KERNEL_TC_PAIRK = 13
+KERNEL_TC_PAIRK, KERNEL_GEMV_TILES = 13, 14
 KERNEL_NAMES = {KERNEL_GEMV_BF16: "gemv_bf16", KERNEL_GEMV_12B: "gemv_12b", KERNEL_TC_TILE: "tc_tile",
                 KERNEL_TC_STREAMK: "tc_streamk", KERNEL_TC_GEMM: "tc_gemm", KERNEL_TC_GEMM2: "tc_gemm2",
                 KERNEL_TC_12B: "tc_12b", KERNEL_TC_SKINNY: "tc_skinny", KERNEL_F32_GEMV: "f32_gemv",
                 KERNEL_GEMV_12T: "gemv_12t", KERNEL_TC_ROWS: "tc_rows", KERNEL_TC_WIDE: "tc_wide",
-                KERNEL_TC_PAIRK: "tc_pairk"}
+                KERNEL_TC_PAIRK: "tc_pairk", KERNEL_GEMV_TILES: "gemv_tiles"}
 TILE_KERNELS = (KERNEL_TC_TILE, KERNEL_TC_STREAMK, KERNEL_TC_SKINNY, KERNEL_TC_GEMM, KERNEL_TC_GEMM2, KERNEL_TC_ROWS,
-                KERNEL_TC_WIDE, KERNEL_TC_PAIRK)
+                KERNEL_TC_WIDE, KERNEL_TC_PAIRK, KERNEL_GEMV_TILES)
 KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
 FLAG_GLOBAL_SPLIT = 1
 FLAG_PDL = 2

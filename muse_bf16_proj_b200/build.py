@@ -20,7 +20,7 @@ LIB = os.path.join(LIB_DIR, "libmuse_proj.so")
 SOURCES = ["capi.cu", "codec12.cpp"]
 HEADERS = ["ptx.cuh", "gather.cuh", "gemv.cuh", "gemv12t.cuh", "tc_tile.cuh", "tc_streamk.cuh", "tc_gemm.cuh",
            "tc_gemm2.cuh", "tc12.cuh", "tc_skinny.cuh", "router.cuh", "enc12.cuh", "enc12_core.h", "errors.h", "stream_read.cuh", "tc_rows.cuh", "tc_wide.cuh",
-           "tc_pairk.cuh", "tc_pairsk.cuh"]
+           "tc_pairk.cuh", "tc_pairsk.cuh", "gemv_tiles.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

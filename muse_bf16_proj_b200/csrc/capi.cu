@@ -28,6 +28,7 @@
 #include "tc_wide.cuh"
 #include "tc_pairk.cuh"
 #include "tc_pairsk.cuh"
+#include "gemv_tiles.cuh"
 
 #define MUSE_VERSION_STRING "muse_proj_b200 0.1 (sm_100a)"
 
@@ -1358,6 +1359,116 @@ int run_gemv12t(const void* tiles12, const MuseEnc12* enc, const void* x, void* 
   }
 }
 
+struct GtShape {
+  int mt, qw, nkb, quads, split, warps, groups, grid, smem;
+};
+
+// A warp takes qw adjacent quads (4 W rows each; plan->chunk: 1, 2, 4 or 8 (M <= 2), 0 = 2) over one of `split` K
+// segments (0: as many as leave each warp at least two batches, a divisor of the CTA's warps);
+// `warps` warps a CTA (0: 8).
+int gt_shape(int64_t m, int64_t n, int64_t k, const MusePlan& p, GtShape* out) {
+  DeviceInfo* d;
+  int limit = kSmemLimit;
+  if (device_info(&d) == MUSE_OK) limit = std::min(kSmemLimit, d->smem_optin);
+  muse::clear_error();
+  if (m < 1 || m > 4) return fail(MUSE_ERR_SHAPE, "gemv_tiles: M must be 1..4 (got %lld)", (long long)m);
+  if (n > (int64_t(1) << 28) || k > (int64_t(1) << 24))
+    return fail(MUSE_ERR_SHAPE, "gemv_tiles: N must be below 2^28 and K below 2^24");
+  GtShape g;
+  g.qw = p.chunk > 0 ? p.chunk : 2;
+  if (g.qw != 1 && g.qw != 2 && g.qw != 4 && g.qw != 8)
+    return fail(MUSE_ERR_PLAN, "gemv_tiles: quads a warp (chunk) must be 1, 2, 4 or 8 (got %d)", g.qw);
+  if (g.qw == 8 && m > 2)
+    return fail(MUSE_ERR_PLAN, "gemv_tiles: 8 quads a warp only for M <= 2 (its accumulators need the registers)");
+  g.warps = p.warps > 0 ? p.warps : 8;
+  if (g.warps > 16) return fail(MUSE_ERR_PLAN, "gemv_tiles: at most 16 warps a CTA (got %d)", g.warps);
+  g.nkb = static_cast<int>((k + 63) / 64);
+  g.split = p.split;
+  const int batch_kb = muse::kGtBatch / g.qw;  // k blocks a batch
+  if (g.split <= 0) {
+    g.split = 1;
+    while (g.warps % (2 * g.split) == 0 && g.nkb / (2 * g.split) >= 2 * batch_kb) g.split *= 2;
+  }
+  if (g.warps % g.split != 0)
+    return fail(MUSE_ERR_PLAN, "gemv_tiles: split %d must divide the %d warps of a CTA", g.split, g.warps);
+  if (g.split > g.nkb) return fail(MUSE_ERR_PLAN, "gemv_tiles: split %d exceeds the %d k blocks", g.split, g.nkb);
+  g.mt = m == 1 ? 1 : (m == 2 ? 2 : 4);
+  g.smem = muse::gt_smem(g.mt, g.qw, g.nkb, g.warps, g.split);
+  if (g.smem > limit)
+    return fail(MUSE_ERR_SHAPE, "gemv_tiles: x of %d tokens x %d k blocks needs %d bytes of shared memory (limit %d)",
+                g.mt, g.nkb, g.smem, limit);
+  g.quads = static_cast<int>((n + 127) / 128) * 32;
+  g.groups = g.warps / g.split;
+  const int per_cta = g.groups * g.qw;
+  g.grid = (g.quads + per_cta - 1) / per_cta;
+  *out = g;
+  return MUSE_OK;
+}
+
+template <int MT, int QW>
+int launch_gemv_tiles(const muse::GtArgs& a, const GtShape& g, bool pdl, cudaStream_t st) {
+  auto kern = muse::gemv_tiles_kernel<MT, QW>;
+  static bool configured[kMaxDevices] = {};
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaError_t e = cudaSuccess;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "cudaFuncSetAttribute(gemv_tiles): %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(g.grid), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(g.warps * 32), 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(g.smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) return fail(MUSE_ERR_CUDA, "gemv_tiles launch: %s", cudaGetErrorString(e));
+  return MUSE_OK;
+}
+
+template <int MT>
+int launch_gemv_tiles_qw(const muse::GtArgs& a, const GtShape& g, bool pdl, cudaStream_t st) {
+  switch (g.qw) {
+    case 1: return launch_gemv_tiles<MT, 1>(a, g, pdl, st);
+    case 2: return launch_gemv_tiles<MT, 2>(a, g, pdl, st);
+    case 4: return launch_gemv_tiles<MT, 4>(a, g, pdl, st);
+    default:
+      if constexpr (MT <= 2) return launch_gemv_tiles<MT, 8>(a, g, pdl, st);
+      return fail(MUSE_ERR_PLAN, "gemv_tiles: 8 quads a warp only for M <= 2");
+  }
+}
+
+int run_gemv_tiles(const void* x, const void* tiles, void* y, int64_t m, int64_t n, int64_t k, const MusePlan& p,
+                   cudaStream_t st) {
+  GtShape g;
+  if (int rc = gt_shape(m, n, k, p, &g)) return rc;
+  muse::GtArgs a;
+  a.tiles = static_cast<const uint8_t*>(tiles);
+  a.x = static_cast<const uint16_t*>(x);
+  a.y = static_cast<uint16_t*>(y);
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.K = static_cast<int>(k);
+  a.nkb = g.nkb;
+  a.quads = g.quads;
+  a.split = g.split;
+  a.groups = g.groups;
+  a.trace = g_trace.load();
+  a.trace_cap = a.trace ? g_trace_cap.load() : 0;
+  const bool pdl = (p.flags & MUSE_FLAG_PDL) != 0;
+  switch (g.mt) {
+    case 1: return launch_gemv_tiles_qw<1>(a, g, pdl, st);
+    case 2: return launch_gemv_tiles_qw<2>(a, g, pdl, st);
+    default: return launch_gemv_tiles_qw<4>(a, g, pdl, st);
+  }
+}
+
 int run_skinny(bool twelve, const void* w, const MuseEnc12* enc, const void* x, void* y, int64_t m, int64_t n,
                int64_t k, const MusePlan& p, void* scratch, int64_t scratch_bytes, cudaStream_t st) {
   SnShape sh;
@@ -1702,6 +1813,10 @@ int muse_scratch_bytes(int64_t m, int64_t n, int64_t k, const MusePlan* plan, in
     RwShape rw;
     return rw_shape(m, n, k, *plan, &rw);
   }
+  if (plan->kernel == MUSE_KERNEL_GEMV_TILES) {  // no scratch: checks the plan only
+    GtShape g;
+    return gt_shape(m, n, k, *plan, &g);
+  }
   if (plan->kernel != MUSE_KERNEL_TC_TILE) return MUSE_OK;
   TcShape sh;
   if (int rc = tc_shape(m, n, k, *plan, &sh)) return rc;
@@ -1726,13 +1841,14 @@ int muse_proj_bf16_tiles(const void* x, const void* tiles, void* y, int64_t m, i
   if (plan->kernel == MUSE_KERNEL_TC_ROWS)
     return run_rows(x, tiles, nullptr, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_WIDE) return run_wide(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
+  if (plan->kernel == MUSE_KERNEL_GEMV_TILES) return run_gemv_tiles(x, tiles, y, m, n, k, *plan, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_PAIRK && (plan->flags & MUSE_FLAG_STREAMK))
     return run_pairsk(x, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
   if (plan->kernel == MUSE_KERNEL_TC_PAIRK)
     return run_pairk(x, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
   if (plan->kernel != MUSE_KERNEL_TC_TILE)
     return fail(MUSE_ERR_PLAN, "proj_bf16_tiles: plan kernel must be TC_TILE, TC_STREAMK, TC_SKINNY, TC_GEMM, TC_GEMM2, "
-                               "TC_ROWS, TC_WIDE or TC_PAIRK");
+                               "TC_ROWS, TC_WIDE, TC_PAIRK or GEMV_TILES");
   return run_tc_tile(x, nullptr, tiles, y, m, n, k, *plan, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 

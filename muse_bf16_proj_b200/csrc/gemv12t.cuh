@@ -45,15 +45,6 @@ __host__ __device__ constexpr int g12_smem(int stages, int ucap, int mt) {
   return 128 + stages * kT12Block + mt * ucap * 64 * 2 + 2 * stages * 8 + 16;
 }
 
-// acc_even += w.lo * x.lo, acc_odd += w.hi * x.hi for two BF16 pairs, each product exact and each
-// sum rounded once to FP32 (mixed-precision FMA: the same numbers as widening both to FP32 first).
-__device__ __forceinline__ void fma_bf16x2(uint32_t w2, uint32_t x2, float& acc_even, float& acc_odd) {
-  asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\tmov.b32 {wl, wh}, %2;\n\tmov.b32 {xl, xh}, %3;\n\t"
-      "fma.rn.f32.bf16 %0, wl, xl, %0;\n\tfma.rn.f32.bf16 %1, wh, xh, %1;\n\t}"
-      : "+f"(acc_even), "+f"(acc_odd)
-      : "r"(w2), "r"(x2));
-}
-
 // One block: this thread's row r, 64 weights, against x[m * xstride + xk ..  + 63] (BF16, shared).
 template <int MT>
 __device__ __forceinline__ void g12_block(const uint8_t* blk, const uint16_t* xs, int xstride, int xk, int r, int M,

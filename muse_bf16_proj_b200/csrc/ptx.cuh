@@ -568,11 +568,45 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
+// acc_even += w.lo * x.lo, acc_odd += w.hi * x.hi for two BF16 pairs, each product exact and each
+// sum rounded once to FP32 (mixed-precision FMA: the same numbers as widening both to FP32 first).
+__device__ __forceinline__ void fma_bf16x2(uint32_t w2, uint32_t x2, float& acc_even, float& acc_odd) {
+  asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\tmov.b32 {wl, wh}, %2;\n\tmov.b32 {xl, xh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, wl, xl, %0;\n\tfma.rn.f32.bf16 %1, wh, xh, %1;\n\t}"
+      : "+f"(acc_even), "+f"(acc_odd)
+      : "r"(w2), "r"(x2));
+}
+
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 v;
   asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
+  return v;
+}
+
+// 16 bytes of streamed read-only data (weights): not kept in L1, L2 eviction by `policy`.
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p, uint64_t policy) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(policy));
+  return v;
+}
+
+// 16 bytes cached in L2 only: data the previous grid may have written (read after its wait).
+__device__ __forceinline__ uint4 ldg_cg_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4u(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
 

@@ -47,6 +47,13 @@ def candidates(m: int, n: int, k: int, sms: int, twelve_ok: bool) -> list[tuple[
     if m <= 4 and k % 256 == 0:
         for warps, ctas in ((16, sms), (16, 2 * sms), (8, 2 * sms)):
             out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_GEMV_BF16, warps=warps, ctas=ctas, chunk=16)))
+    if m <= 4:  # the register-streaming GEMV over the packed tiles (split 0: about 16 k blocks a warp)
+        nkb = (k + 63) // 64
+        for qw in (1, 2, 4, 8):
+            for warps, split in ((8, 0), (4, 0), (16, 0), (8, 1), (16, 2), (16, 4), (8, 4), (4, 4), (16, 8)):
+                if split <= nkb and (qw < 8 or m <= 2) and (qw > 1 or warps != 16 or split != 8):
+                    out.append(("bf16", _lib.MusePlan(kernel=_lib.KERNEL_GEMV_TILES, warps=warps, split=split,
+                                                      chunk=qw)))
     if twelve_ok and m <= 4:
         for warps, ctas in ((8, 2 * sms), (16, sms), (16, 2 * sms)):
             out.append(("12b", _lib.MusePlan(kernel=_lib.KERNEL_GEMV_12B, warps=warps, ctas=ctas)))
@@ -379,7 +386,8 @@ def main():
     ap.add_argument("--no-12b", action="store_true")
     ap.add_argument("--out", default="sweep.json")
     ap.add_argument("--write-table", action="store_true")
-    ap.add_argument("--merge", action="store_true", help="with --write-table / --from-json: replace only the swept shapes")
+    ap.add_argument("--merge", action="store_true",
+                    help="with --write-table / --from-json: replace only the swept shapes' rows up to the largest swept M")
     ap.add_argument("--plan", default="", help='time only this plan, e.g. {"kernel": "tc_tile", "split": 3}')
     ap.add_argument("--trace", action="store_true", help="also record per-CTA timestamps of each plan")
     ap.add_argument("--flags", type=int, default=0, help="plan flags OR-ed into every candidate (2 = PDL)")
@@ -391,7 +399,7 @@ def main():
     if args.from_json:
         with open(args.from_json) as f:
             done = json.load(f)
-        write_table(done["rows"], done.get("device", "?"), print, args.merge)
+        write_table(done["rows"], done.get("device", "?"), print, args.merge, args.no_12b)
         return
     torch.backends.cuda.matmul.allow_tf32 = False
     only = None
@@ -430,22 +438,51 @@ def main():
         json.dump({"device": torch.cuda.get_device_name(), "sms": sms, "rows": rows,
                    "seconds": time.time() - t0}, f)
     if args.write_table:
-        write_table(rows, torch.cuda.get_device_name(), log, args.merge)
+        write_table(rows, torch.cuda.get_device_name(), log, args.merge, args.no_12b)
 
 
-def merge_entries(old: list, new: list) -> list:
-    """The committed table's rows with every (N, K) shape that `new` covers replaced by `new`'s rows
-    (a targeted re-sweep updates its shapes and keeps the rest), sorted by shape, format and M."""
-    swept = {(e["n"], e["k"]) for e in new}
-    kept = [e for e in old if (e["n"], e["k"]) not in swept]
+def merge_entries(old: list, new: list, bf16_only: bool = False) -> list:
+    """The committed table's rows with the swept ones replaced: for every (N, K) shape that `new`
+    covers, the old rows for M up to the largest M `new` covers are dropped (a row reaching past it
+    is cut to start above it) and `new`'s rows take their place; other shapes and larger M keep
+    their rows, so a targeted re-sweep of a few shapes or of small M updates only those. With
+    `bf16_only` (a sweep without 12-bit candidates) an old 12-bit row in the swept range stays if
+    it beats the new BF16 row at every M both timed. Sorted by shape, format and M."""
+    top: dict = {}
+    for e in new:
+        top[(e["n"], e["k"])] = max(top.get((e["n"], e["k"]), 0), e["m_hi"])
+
+    def new_us(key, m):
+        for e in new:
+            if (e["n"], e["k"]) == key and e["m_lo"] <= m <= e["m_hi"] and str(m) in e["us"]:
+                return e["us"][str(m)]
+        return None
+
+    kept = []
+    for e in old:
+        key = (e["n"], e["k"])
+        if key not in top or e["m_lo"] > top[key]:
+            kept.append(e)
+            continue
+        if bf16_only and e.get("weights") == "12b":
+            pairs = [(t, new_us(key, int(m))) for m, t in e["us"].items() if int(m) <= top[key]]
+            if pairs and all(u is not None and t < u for t, u in pairs):
+                kept.append(e)
+                continue
+        if e["m_hi"] > top[key]:
+            cut = {**e, "m_lo": top[key] + 1}
+            for field in ("us", "cublas_us"):
+                if field in e:
+                    cut[field] = {m: t for m, t in e[field].items() if int(m) > top[key]}
+            kept.append(cut)
     return sorted(kept + list(new), key=lambda e: (e["n"], e["k"], e.get("weights", "bf16"), e["m_lo"]))
 
 
-def write_table(rows, device: str, log, merge: bool = False) -> None:
+def write_table(rows, device: str, log, merge: bool = False, bf16_only: bool = False) -> None:
     entries = table_entries(rows)
     if merge and os.path.exists(TABLE_PATH):
         with open(TABLE_PATH) as f:
-            entries = merge_entries(json.load(f).get("entries", []), entries)
+            entries = merge_entries(json.load(f).get("entries", []), entries, bf16_only)
     table = {"generated_by": "python -m muse_bf16_proj_b200.sweep --write-table [--merge] (or --from-json of its output)",
              "device": device,
              "timing": ("us = mean per launch of back-to-back launches (programmatic launch), weights cold in L2; "

@@ -208,6 +208,27 @@ def test_pair_kernel_plans_and_scratch():
         _lib.scratch_bytes(512, 57344, 8192, sk)
 
 
+def test_tile_gemv_plan_checks():
+    """The decode tile GEMV needs no scratch and refuses plans it cannot run, on the host."""
+    gt = lambda **kw: _lib.MusePlan(kernel=_lib.KERNEL_GEMV_TILES, **kw)
+    for m in (1, 2, 3, 4):
+        assert _lib.scratch_bytes(m, 6144, 4096, gt()) == 0
+    assert _lib.scratch_bytes(1, 6144, 4096, gt(warps=16, split=16)) == 0
+    assert _lib.scratch_bytes(1, 130, 136, gt(warps=4, split=2)) == 0
+    assert _lib.scratch_bytes(4, 6144, 4096, gt(warps=16, split=4, chunk=4)) == 0
+    assert _lib.scratch_bytes(2, 6144, 4096, gt(warps=8, split=4, chunk=8)) == 0
+    for m, n, k, plan, code in ((5, 6144, 4096, gt(), -3),                     # at most 4 tokens
+                                (1, 6144, 4096, gt(warps=8, split=3), -7),     # split divides the warps
+                                (1, 6144, 4096, gt(warps=17), -7),             # at most 16 warps
+                                (1, 6144, 4096, gt(chunk=3), -7),              # 1, 2, 4 or 8 quads a warp
+                                (3, 6144, 4096, gt(chunk=8), -7),              # 8 only for M <= 2
+                                (1, 6144, 128, gt(warps=8, split=4), -7),      # split <= k blocks (2)
+                                (4, 6144, 1 << 16, gt(), -3)):                  # x must fit shared memory
+        with pytest.raises(_lib.MuseError) as e:
+            _lib.scratch_bytes(m, n, k, plan)
+        assert e.value.code == code, (m, n, k, plan.as_dict())
+
+
 def test_device_encoder_argument_errors():
     """muse_encode12_device / _escapes reject bad shapes, null or misaligned pointers before any launch."""
     lib = _lib.load()

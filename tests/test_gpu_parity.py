@@ -133,6 +133,37 @@ def test_gemv_bf16_plan_variants_and_determinism():
     assert np.array_equal(again, outs[0])
 
 
+GT_SHAPES = GEMV_SHAPES + [(130, 136), (4100, 8192)]
+
+
+@pytest.mark.parametrize("n,k", GT_SHAPES)
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+def test_gemv_tiles(n, k, m):
+    """The decode GEMV over packed tiles: ragged N (not a multiple of 4 or 128) and K (not a multiple
+    of 64), every token count, the default plan and explicit warp / split layouts."""
+    xb, wb = _rand_bits((m, k), 11 + m), _rand_bits((n, k), 12 + n, 0.02)
+    nkb = (k + 63) // 64
+    plans = [{}] + [{"warps": w, "split": s, "chunk": q} for w, s, q in
+                    ((4, 1, 1), (8, 2, 1), (8, 8, 2), (16, 16, 1), (8, 2, 4), (16, 4, 4), (4, 4, 2), (8, 4, 8))
+                    if s <= nkb and (q < 8 or m <= 2)]
+    for d in plans:
+        plan = _lib.MusePlan.from_dict({"kernel": "gemv_tiles", **d})
+        assert_parity(xb, wb, _run_bf16(xb, wb, plan, tiles=True), what=f"gemv_tiles n={n} k={k} m={m} {d}")
+
+
+def test_gemv_tiles_subset_rows_and_determinism():
+    """W[:n] of a larger packed W (the row tiles past n are never read for output), and the same
+    bits on every call."""
+    m, k = 3, 4096
+    xb, wb = _rand_bits((m, k), 21), _rand_bits((1024, k), 22, 0.02)
+    plan = _lib.MusePlan(kernel=_lib.KERNEL_GEMV_TILES, flags=_lib.FLAG_PDL)
+    y = _run_bf16(xb, wb, plan, n=1000, tiles=True)
+    assert_parity(xb, wb, y, n=1000, what="gemv_tiles W[:1000]")
+    first = bits(y)
+    for _ in range(3):
+        assert np.array_equal(bits(_run_bf16(xb, wb, plan, n=1000, tiles=True)), first)
+
+
 TC_CASES = [  # (m, n, k, tile_n, split)
     (16, 6144, 4096, 16, 3), (16, 6144, 4096, 16, 1), (1, 6144, 4096, 16, 4), (8, 2304, 8192, 16, 8),
     (5, 1024, 4096, 16, 16), (32, 4096, 8192, 32, 4), (33, 8192, 1024, 64, 2), (130, 8192, 4096, 256, 1),
@@ -288,12 +319,15 @@ def test_cuda_graph_replay_with_fresh_inputs(state, ref_weights):
     {"kernel": "tc_tile", "tile_n": 16, "split": 4, "flags": 1 | 2},
     {"kernel": "tc_tile", "tile_n": 32, "split": 1, "flags": 2},
     {"kernel": "gemv_bf16", "warps": 8, "flags": 2},
+    {"kernel": "gemv_tiles", "flags": 2},
+    {"kernel": "gemv_tiles", "warps": 16, "split": 8, "flags": 2},
+    {"kernel": "gemv_tiles", "warps": 8, "split": 2, "chunk": 4, "flags": 2},
 ])
 def test_programmatic_launch_chain(plan_dict):
     """Each projection feeds the next (square W): with programmatic launch a kernel must still read
     the previous kernel's finished output. Same bits as the plain launches."""
     n = k = 1024
-    m = 8 if plan_dict["kernel"] == "gemv_bf16" else 16
+    m = {"gemv_bf16": 8, "gemv_tiles": 4}.get(plan_dict["kernel"], 16)
     wb = _rand_bits((n, k), 61, 1.0 / 32)
     w = to_dev(wb)
     t = torch.empty(_lib.tiles_bytes(n, k), dtype=torch.uint8, device="cuda")

@@ -50,3 +50,28 @@ def test_merge_replaces_only_the_swept_shapes():
     new = [{"n": 20, "k": 512, "m_lo": 1, "m_hi": 8, "weights": "12b", "plan": {"kernel": "gemv_12t"}}]
     got = merge_entries(old, new)
     assert [(e["n"], e["weights"], e["plan"]["kernel"]) for e in got] == [(10, "bf16", "tc_tile"), (20, "12b", "gemv_12t")]
+
+
+def test_merge_of_a_small_m_sweep_keeps_larger_m_and_faster_12b_rows():
+    from muse_bf16_proj_b200.sweep import merge_entries
+    old = [{"n": 20, "k": 512, "m_lo": 1, "m_hi": 2, "weights": "12b", "plan": {"kernel": "gemv_12t"}, "us": {"1": 5.0, "2": 6.0}},
+           {"n": 20, "k": 512, "m_lo": 3, "m_hi": 4, "weights": "12b", "plan": {"kernel": "gemv_12b"}, "us": {"4": 9.0}},
+           {"n": 20, "k": 512, "m_lo": 1, "m_hi": 8, "weights": "bf16", "plan": {"kernel": "tc_tile"},
+            "us": {"1": 8.0, "2": 8.0, "4": 8.0, "8": 9.0}, "cublas_us": {"1": 10.0, "8": 11.0}},
+           {"n": 20, "k": 512, "m_lo": 9, "m_hi": 16, "weights": "bf16", "plan": {"kernel": "tc_tile", "split": 2},
+            "us": {"16": 10.0}}]
+    new = [{"n": 20, "k": 512, "m_lo": 1, "m_hi": 4, "weights": "bf16", "plan": {"kernel": "gemv_tiles"},
+            "us": {"1": 5.5, "2": 6.5, "4": 7.0}}]
+    got = merge_entries(old, new, bf16_only=True)
+    rows = [(e["weights"], e["m_lo"], e["m_hi"], e["plan"]["kernel"]) for e in got]
+    # The 12-bit row faster at M = 1, 2 stays; the one slower at M = 4 goes; the old BF16 row is cut
+    # to start above the swept range, keeping only its timings there; M > 8 is untouched.
+    assert rows == [("12b", 1, 2, "gemv_12t"), ("bf16", 1, 4, "gemv_tiles"), ("bf16", 5, 8, "tc_tile"),
+                    ("bf16", 9, 16, "tc_tile")]
+    cut = got[2]
+    assert cut["us"] == {"8": 9.0} and cut["cublas_us"] == {"8": 11.0}
+    assert old[2]["m_lo"] == 1  # the committed rows are not modified in place
+    d = Dispatch(entries=got)
+    assert d.plan(1, 20, 512, have_12b=True)[1] == "12b"
+    assert d.plan(3, 20, 512, have_12b=True)[0].kernel == _lib.KERNEL_GEMV_TILES
+    assert d.plan(6, 20, 512)[0].kernel == _lib.KERNEL_TC_TILE
