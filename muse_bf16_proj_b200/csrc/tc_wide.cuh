@@ -250,8 +250,9 @@ __global__ void __launch_bounds__(kWdThreads, 1)
             asm volatile("bar.sync 1, 128;" ::: "memory");
             if (threadIdx.x == 64) {
               const int row0 = mt * 256 + static_cast<int>(rank) * 128;
-              tma_store_2d(&tmy, ystg, n0 + r * 128, row0);
-              tma_store_2d(&tmy, ystg + 16384, n0 + r * 128 + 64, row0);
+              const uint64_t pol_y = policy_evict_first();  // written once, never re-read here
+              tma_store_2d_hint(&tmy, ystg, n0 + r * 128, row0, pol_y);
+              tma_store_2d_hint(&tmy, ystg + 16384, n0 + r * 128 + 64, row0, pol_y);
               bulk_commit();
             }
           }
