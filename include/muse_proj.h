@@ -157,7 +157,8 @@ int muse_device_error(int* code, void* stream);
 /*
  * The library's default plan for a shape and weight format (MUSE_WEIGHTS_*). Replaces the
  * reference's per-shape tables' fallback rule (submission.py:76-127, 900-908): shapes no table
- * row names get this plan.
+ * row names get this plan. Packed tiles: GEMV_TILES at M <= 2 (when x fits its shared memory),
+ * stream-K up to 128 tokens, the pair GEMMs above 256.
  */
 int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* out);
 

@@ -1614,6 +1614,18 @@ int muse_plan_default(int64_t m, int64_t n, int64_t k, int weights, MusePlan* ou
   }
   int bnt = 16;
   while (bnt < m && bnt < 256) bnt *= 2;
+  if (weights == MUSE_WEIGHTS_TILES && m <= 2) {
+    // One or two tokens: the register-streaming GEMV, 8 adjacent quads (4 KB) a warp, 4 warps a CTA
+    // (measured on a B200 ahead of every tensor-core plan at M <= 2 on every swept shape), when x fits
+    // its shared memory.
+    out->kernel = MUSE_KERNEL_GEMV_TILES;
+    out->warps = 4;
+    out->chunk = 8;
+    GtShape g;
+    if (gt_shape(m, n, k, *out, &g) == MUSE_OK) return MUSE_OK;
+    muse::clear_error();
+    std::memset(out, 0, sizeof(*out));
+  }
   if (weights == MUSE_WEIGHTS_TILES && m <= 128) {
     // Stream-K: every SM streams the same share of W in one wave.
     out->kernel = MUSE_KERNEL_TC_STREAMK;

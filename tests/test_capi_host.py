@@ -70,7 +70,11 @@ def test_plan_default_without_device():
     p = _lib.plan_default(1, 6144, 4096)
     assert p.kernel == _lib.KERNEL_GEMV_BF16
     p = _lib.plan_default(1, 6144, 4096, tiles=True)
+    assert p.kernel == _lib.KERNEL_GEMV_TILES and p.chunk == 8 and p.warps == 4
+    p = _lib.plan_default(3, 6144, 4096, tiles=True)
     assert p.kernel == _lib.KERNEL_TC_STREAMK and p.tile_n == 16
+    p = _lib.plan_default(2, 6144, 1 << 20, tiles=True)  # x past the GEMV's shared memory: stream-K
+    assert p.kernel == _lib.KERNEL_TC_STREAMK
     p = _lib.plan_default(16, 6144, 4096)
     assert p.kernel == _lib.KERNEL_TC_TILE and p.tile_n == 16 and 1 <= p.split <= 8
     p = _lib.plan_default(200, 6144, 4096, tiles=True)

@@ -164,6 +164,17 @@ def test_gemv_tiles_subset_rows_and_determinism():
         assert np.array_equal(bits(_run_bf16(xb, wb, plan, n=1000, tiles=True)), first)
 
 
+def test_default_plan_at_one_and_two_tokens():
+    """A shape no table row names takes the library's default plan: the tile GEMV at M <= 2."""
+    n, k = 3000, 2048
+    wb = _rand_bits((n, k), 31, 0.02)
+    for m in (1, 2):
+        plan = _lib.plan_default(m, n, k, tiles=True)
+        assert plan.kernel == _lib.KERNEL_GEMV_TILES
+        xb = _rand_bits((m, k), 32 + m)
+        assert_parity(xb, wb, _run_bf16(xb, wb, plan, tiles=True), what=f"default plan m={m}")
+
+
 TC_CASES = [  # (m, n, k, tile_n, split)
     (16, 6144, 4096, 16, 3), (16, 6144, 4096, 16, 1), (1, 6144, 4096, 16, 4), (8, 2304, 8192, 16, 8),
     (5, 1024, 4096, 16, 16), (32, 4096, 8192, 32, 4), (33, 8192, 1024, 64, 2), (130, 8192, 4096, 256, 1),
